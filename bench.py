@@ -1,0 +1,447 @@
+"""Benchmark of the sequence-parallel attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {ours,reference}]
+
+Headline (``value``): causal zigzag ring-attention prefill, LLaMA-3-8B
+attention shape (B=1, 32 query / 8 KV heads, D=128, 131072 tokens, bf16),
+total sequence split over N ranks - TFLOP/s of algorithmic work (visible
+(q, k) pairs x 4 x D x Hq) for the whole job.  Inputs (1.25 GiB) exceed L2, so
+no flush is needed between steps.  Side metric (``decode``): split-KV decode,
+B=16, 32/8 heads, 131072-token bf16 cache sharded over the ranks, 256 steps
+each appending one token to the last rank's shard - tokens/s and HBM GB/s.
+
+``e2e`` repeats the prefill through the public API with inputs copied from
+pinned host memory and the output copied back inside the timed region.
+``--impl reference`` times the reference algorithm's CPU restatement
+(``oracle/``, numpy + OpenBLAS, all host threads) on a bounded sample of the
+same workload; rank 0 alone runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+S_TOTAL, HQ, HKV, D = 131072, 32, 8, 128
+DEC_B, DEC_T, DEC_STEPS, DEC_WARM = 16, 131072, 256, 8
+METRIC = "causal SP prefill attention TFLOP/s at 1/2/4/8 B200; split-KV decode tok/s"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def _traffic_summary():
+    """Per-launch DRAM bytes of the dominant kernels from a committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed set-up
+def setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    return rank, world, dev
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def visible_pairs(pos: torch.Tensor) -> int:
+    """Causal (q, k) pairs of a prefix-complete sequence: query at position p sees p + 1 keys."""
+    return int((pos.to(torch.int64) + 1).sum().item())
+
+
+# ----------------------------------------------------------------------------- ours: prefill
+def bench_prefill(cea, rank, world, dev, steps, warmup):
+    from collaborative_edge_system_b200 import sequence_parallel as sp_mod
+
+    layout = cea.SequenceLayout(S_TOTAL, world, None, "zigzag")
+    idx = layout.indices(rank)
+    pos = idx.view(1, -1).to(dev)
+    s_loc = layout.sizes[rank]
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    q = (torch.randn(1, s_loc, HQ, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    k = torch.randn(1, s_loc, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, s_loc, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    comm = cea.ParallelContext(1, world, 1, device=dev).sp
+    scale = 1.0 / math.sqrt(D)
+    total_flops = 4.0 * HQ * D * (S_TOTAL * (S_TOTAL + 1) / 2)
+    my_flops = 4.0 * HQ * D * visible_pairs(idx)
+
+    # instrument the attention launches (events on the launching stream) without changing the step
+    from collaborative_edge_system_b200 import attention as attn_mod
+
+    orig = attn_mod.attend_into
+    ev = []
+
+    def timed_attend(*a, **kw):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        orig(*a, **kw)
+        e.record()
+        ev.append((s, e))
+
+    def step():
+        return cea.ring_attention(q, k, v, pos, pos, comm, layout.sizes, causal=True, scale=scale)
+
+    for _ in range(warmup):
+        step()
+    barrier(world)
+    attn_mod.attend_into = sp_mod.attend_into = timed_attend
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        barrier(world)
+        start.record()
+        for _ in range(steps):
+            step()
+        end.record()
+        barrier(world)
+    attn_mod.attend_into = sp_mod.attend_into = orig
+    launches_before = 0
+    ms = start.elapsed_time(end)
+    ms = max_over_ranks(ms, world, dev)
+    kern_ms = sum(s.elapsed_time(e) for s, e in ev[launches_before:])
+    kern_ms_per_step = kern_ms / steps
+    n_attn = (len(ev) - launches_before) // steps  # attention calls per step
+    # our kernels per attention call: two tile-stat passes + the tcgen05 kernel
+    gpu_launches = steps * n_attn * 3
+    return {
+        "ms_per_step": ms / steps,
+        "tflops": total_flops * steps / (ms / 1e3) / 1e12,
+        "kernel_ms_per_step": kern_ms_per_step,
+        "kernel_tflops_rank": my_flops / (kern_ms_per_step / 1e3) / 1e12,
+        "launches_per_step": n_attn,
+        "gpu_launches": gpu_launches,
+        "clocks": clk.summary(),
+        "layout": layout,
+        "tensors": (q, k, v, pos),
+        "comm": comm,
+        "flops_total": total_flops,
+        "flops_rank": my_flops,
+    }
+
+
+def bench_prefill_e2e(cea, rank, world, dev, steps, warmup, layout, tensors, comm):
+    """Same step through the public API, inputs from pinned host memory, output back to the host."""
+    q, k, v, pos = tensors
+    hq, hk, hv, hp = (t.cpu().pin_memory() for t in (q, k, v, pos))
+    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    scale = 1.0 / math.sqrt(D)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hp))
+    d2h = hout.numel() * hout.element_size()
+
+    def step():
+        dq, dk, dv, dp = (t.to(dev, non_blocking=True) for t in (hq, hk, hv, hp))
+        out = cea.ring_attention(dq, dk, dv, dp, dp, comm, layout.sizes, causal=True, scale=scale)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, warmup // 2)):
+        step()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world, dev)
+    total_flops = 4.0 * HQ * D * (S_TOTAL * (S_TOTAL + 1) / 2)
+    return {"value": total_flops * steps / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms / steps}
+
+
+# ----------------------------------------------------------------------------- ours: decode
+def bench_decode(cea, rank, world, dev):
+    from collaborative_edge_system_b200 import attention as attn_mod
+
+    T_loc = [DEC_T // world + (1 if r < DEC_T % world else 0) for r in range(world)]
+    start_pos = sum(T_loc[:rank])
+    cap = T_loc[rank] + (DEC_STEPS + DEC_WARM if rank == world - 1 else 0)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    kc = torch.randn(DEC_B, HKV, cap, D, generator=g, device=dev).to(torch.bfloat16)  # head-major cache
+    vc = torch.randn(DEC_B, HKV, cap, D, generator=g, device=dev).to(torch.bfloat16)
+    kpos = torch.full((DEC_B, cap), -1, dtype=torch.int64, device=dev)
+    kpos[:, : T_loc[rank]] = torch.arange(start_pos, start_pos + T_loc[rank], device=dev)
+    comm = cea.ParallelContext(1, world, 1, device=dev).sp
+    length = T_loc[rank]
+    owner = world - 1
+    scale = 1.0 / math.sqrt(D)
+    ev = []
+    orig = attn_mod._lib.attn_fwd
+
+    def timed_fwd(p, device, entry="cea_attn_fwd"):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        orig(p, device, entry)
+        e.record()
+        ev.append((s, e))
+
+    state = {"length": length, "pos": DEC_T, "i": 0}
+    qs = torch.randn(8, DEC_B, 1, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+    kvs = torch.randn(8, DEC_B, HKV, 1, D, generator=g, device=dev).to(torch.bfloat16)
+
+    def step():
+        L = state["length"]
+        qpos = torch.full((DEC_B, 1), state["pos"], dtype=torch.int64, device=dev)
+        i = state["i"] = (state["i"] + 1) % 8
+        q = qs[i]
+        if rank == owner:  # the new token's K/V join the last rank's shard
+            kc[:, :, L : L + 1] = kvs[i]
+            vc[:, :, L : L + 1] = kvs[(i + 3) % 8]
+            kpos[:, L] = state["pos"]
+            state["length"] = L = L + 1
+        k_view, v_view = kc[:, :, :L].transpose(1, 2), vc[:, :, :L].transpose(1, 2)
+        out = cea.distributed_kv_attention(q, k_view, v_view, qpos, kpos[:, :L], comm, causal=True, scale=scale)
+        state["pos"] += 1
+        return out
+
+    for _ in range(DEC_WARM):
+        step()
+    barrier(world)
+    attn_mod._lib.attn_fwd = timed_fwd
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(DEC_STEPS):
+        step()
+    t1.record()
+    barrier(world)
+    attn_mod._lib.attn_fwd = orig
+    ms = max_over_ranks(t0.elapsed_time(t1), world, dev)
+    kern_ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
+    avg_len = state["length"] - DEC_STEPS / 2 if rank == owner else state["length"]
+    kv_bytes = 2.0 * DEC_B * HKV * avg_len * D * 2  # K and V read by this rank per step
+    hbm = _peaks()[2]
+    return {
+        "tok_per_s": DEC_B * DEC_STEPS / (ms / 1e3),
+        "ms_per_step": ms / DEC_STEPS,
+        "kernel_ms": kern_ms,
+        "kernel_gbs": kv_bytes / (kern_ms / 1e3) / 1e9,
+        "hbm_frac": kv_bytes / (kern_ms / 1e3) / 1e9 / hbm,
+        "kv_bytes_per_step_rank": kv_bytes,
+    }
+
+
+# ----------------------------------------------------------------------------- CPU baseline (oracle)
+def cpu_baseline(seconds_target: float = 15.0):
+    """The reference algorithm's CPU restatement on a bounded sample of the prefill workload.
+
+    Sample: the last ``nq`` query positions of a causal prefix of ``sk`` tokens,
+    all 32 query heads (GQA 4:1, D=128), fp32 from bf16-rounded inputs; FLOP/s
+    of visible pairs, which converts to the full 131072-token prefill.
+    """
+    import numpy as np
+
+    import oracle
+
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+
+    def run(nq, sk):
+        q = (rng.standard_normal((1, nq, HQ, D)) / math.sqrt(D)).astype(np.float32)
+        k = rng.standard_normal((1, sk, HKV, D)).astype(np.float32)
+        v = rng.standard_normal((1, sk, HKV, D)).astype(np.float32)
+        kp = np.arange(sk).reshape(1, sk)
+        qp = kp[:, sk - nq :]
+        t0 = time.perf_counter()
+        oracle.attention_with_lse(q, k, v, qp, kp, True, 1.0 / math.sqrt(D), None, acc=np.float32)
+        dt = time.perf_counter() - t0
+        pairs = float(((qp + 1).sum()))
+        return 4.0 * HQ * D * pairs, dt
+
+    flops, dt = run(256, 8192)
+    scale = max(1.0, min(64.0, seconds_target / max(dt, 1e-3)))
+    nq = int(min(8192, 256 * scale))
+    nq -= nq % 128
+    flops, dt = run(max(nq, 128), 16384)
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"last {max(nq, 128)} query positions of a 16384-token causal prefix, 32/8 heads, D=128, "
+                      f"fp32 numpy oracle ({dt:.1f} s)"}
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+
+    config = {"workload": "zigzag causal ring-attention prefill, LLaMA-3-8B attention shape",
+              "batch": 1, "seq_len": S_TOTAL, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+              "layout": "zigzag", "parallelism": f"sp{args.gpus}", "l2": "inputs larger than L2 (no flush)"}
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        t0 = time.perf_counter()
+        vals = []
+        for _ in range(max(1, args.warmup // 3) + args.steps):
+            vals.append(cpu_baseline(seconds_target=max(2.0, 60.0 / (args.steps + 1))))
+        base = vals[-1]
+        v = statistics.median(x["value"] for x in vals[-args.steps :])
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "dtype": "f32", "data": "synthetic", "config": config,
+                          "cpu_baseline": {**base, "value": v},
+                          "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                          "wall_s": time.perf_counter() - t0}))
+        return
+
+    import collaborative_edge_system_b200 as cea
+    from collaborative_edge_system_b200 import _lib
+
+    _lib.load()
+    rank, world, dev = setup(args.gpus)
+    warmup = max(3, args.warmup)
+    pre = bench_prefill(cea, rank, world, dev, args.steps, warmup)
+    e2e = bench_prefill_e2e(cea, rank, world, dev, max(1, min(args.steps, 3)), warmup, pre["layout"],
+                            pre["tensors"], pre["comm"])
+    del pre["tensors"]
+    dec = None if args.no_decode else bench_decode(cea, rank, world, dev)
+    status = _lib.device_status(clear=True)
+    peak_burst, peak_sus, hbm, peak_kind = _peaks()
+    traffic = _traffic_summary()
+    kt = pre["kernel_tflops_rank"]
+    line = {
+        "metric": METRIC,
+        "value": pre["tflops"],
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": warmup,
+        "ms_per_step": pre["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1), q scaled by 1/sqrt(128))",
+        "config": config,
+        "roofline": {"bound": "tensor", "kernel": "attn_fwd_tc_kernel", "achieved": kt, "peak": peak_burst,
+                     "unit": "TFLOP/s", "frac": kt / peak_burst, "frac_of_sustained": kt / peak_sus,
+                     "peak_source": peak_kind, "traffic": traffic.get("attn_fwd_tc_kernel_bytes_per_launch"),
+                     "flops_per_launch": pre["flops_rank"] / max(1, pre["launches_per_step"]),
+                     "kernel_ms_per_step": pre["kernel_ms_per_step"]},
+        "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+        "gpu_launches": pre["gpu_launches"],
+        "clocks": {k: pre["clocks"][k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        "device_status": status,
+    }
+    if dec is not None:
+        line["decode"] = {"metric": "split-KV decode tok/s", "value": dec["tok_per_s"], "unit": "tok/s",
+                          "ms_per_step": dec["ms_per_step"], "steps": DEC_STEPS,
+                          "config": {"batch": DEC_B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                                     "cache_tokens": DEC_T, "sharding": "contiguous"},
+                          "roofline": {"bound": "hbm", "kernel": "decode_partial_kernel", "achieved": dec["kernel_gbs"],
+                                       "peak": hbm, "unit": "GB/s", "frac": dec["hbm_frac"],
+                                       "traffic": traffic.get("decode_partial_kernel_bytes_per_launch"),
+                                       "kernel_ms": dec["kernel_ms"]}}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

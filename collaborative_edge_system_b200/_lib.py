@@ -1,0 +1,292 @@
+"""ctypes binding of libcea.so (the C ABI declared in include/cea.h).
+
+Only plain pointers, sizes and strides cross the boundary; PyTorch provides
+device memory and the current CUDA stream.  There is no CPU fallback: a
+missing library or a non-CUDA tensor raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Sequence
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libcea.so")
+
+F32, F16, BF16, F64 = 0, 1, 2, 3
+_DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
+
+CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE = range(6)
+MAX_MERGE = 32
+MAX_SEGMENTS = 64
+
+KIND_NONE, KIND_TC, KIND_DECODE, KIND_SIMT = 0, 1, 2, 3
+
+_i64x2 = ctypes.c_int64 * 2
+_i64x3 = ctypes.c_int64 * 3
+
+
+class AttnParams(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("q_pos", ctypes.c_void_p),
+        ("k_pos", ctypes.c_void_p),
+        ("kv_map", ctypes.c_void_p),
+        ("q_stride", _i64x3),
+        ("k_stride", _i64x3),
+        ("v_stride", _i64x3),
+        ("o_stride", _i64x3),
+        ("lse_stride", _i64x3),
+        ("qpos_stride", _i64x2),
+        ("kpos_stride", _i64x2),
+        ("B", ctypes.c_int32),
+        ("Sq", ctypes.c_int32),
+        ("Sk", ctypes.c_int32),
+        ("Hq", ctypes.c_int32),
+        ("Hkv", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("scale", ctypes.c_double),
+        ("causal", ctypes.c_int32),
+        ("in_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
+        ("accumulate", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class MergeParams(ctypes.Structure):
+    _fields_ = [
+        ("n", ctypes.c_int32),
+        ("outs", ctypes.c_void_p * MAX_MERGE),
+        ("lses", ctypes.c_void_p * MAX_MERGE),
+        ("out", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("part_o_stride", _i64x3),
+        ("part_lse_stride", _i64x3),
+        ("o_stride", _i64x3),
+        ("lse_stride", _i64x3),
+        ("B", ctypes.c_int32),
+        ("Sq", ctypes.c_int32),
+        ("H", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("part_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
+    ]
+
+
+class Segment(ctypes.Structure):
+    _fields_ = [
+        ("src", ctypes.c_void_p),
+        ("dst", ctypes.c_void_p),
+        ("src_stride", _i64x3),
+        ("dst_stride", _i64x3),
+        ("nb", ctypes.c_int32),
+        ("ns", ctypes.c_int32),
+        ("nh", ctypes.c_int32),
+    ]
+
+
+class CopyParams(ctypes.Structure):
+    _fields_ = [
+        ("n", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("elem_bytes", ctypes.c_int32),
+        ("seg", Segment * MAX_SEGMENTS),
+    ]
+
+
+EXPORTS = (
+    "cea_attn_fwd",
+    "cea_attn_workspace_size",
+    "cea_attn_kernel_kind",
+    "cea_decode_splitkv",
+    "cea_merge",
+    "cea_ulysses_pack",
+    "cea_ulysses_unpack",
+    "cea_device_status",
+    "cea_last_error",
+    "cea_abi_version",
+)
+
+_lib: Optional[ctypes.CDLL] = None
+_lock = threading.Lock()
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libcea.so once; raises if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"{path} is missing: build it with `python -m collaborative_edge_system_b200.build` "
+                "(the sequence-parallel attention kernels have no CPU fallback)"
+            )
+        lib = ctypes.CDLL(path)
+        P = ctypes.c_void_p
+        for name, args, res in (
+            ("cea_attn_fwd", [ctypes.POINTER(AttnParams), P], ctypes.c_int),
+            ("cea_decode_splitkv", [ctypes.POINTER(AttnParams), P], ctypes.c_int),
+            ("cea_attn_workspace_size", [ctypes.POINTER(AttnParams)], ctypes.c_size_t),
+            ("cea_attn_kernel_kind", [ctypes.POINTER(AttnParams)], ctypes.c_int),
+            ("cea_merge", [ctypes.POINTER(MergeParams), P], ctypes.c_int),
+            ("cea_ulysses_pack", [ctypes.POINTER(CopyParams), P], ctypes.c_int),
+            ("cea_ulysses_unpack", [ctypes.POINTER(CopyParams), P], ctypes.c_int),
+            ("cea_device_status", [ctypes.POINTER(ctypes.c_int), ctypes.c_int, P], ctypes.c_int),
+            ("cea_last_error", [], ctypes.c_char_p),
+            ("cea_abi_version", [], ctypes.c_int),
+        ):
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        if lib.cea_abi_version() != 1:
+            raise RuntimeError("libcea.so ABI version mismatch; rebuild it")
+        _lib = lib
+        return lib
+
+
+def _check(code: int, what: str) -> None:
+    if code == CEA_OK:
+        return
+    msg = load().cea_last_error().decode(errors="replace")
+    if code in (CEA_ERR_INVALID,):
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what} failed ({code}): {msg}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}") from None
+
+
+def require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise ValueError(
+                f"the B200 attention kernels need CUDA tensors, got a tensor on {t.device} "
+                "(there is no CPU path; move the inputs to the GPU)"
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def attn_params(
+    q, k, v, q_pos, k_pos, out, lse, *, causal: bool, scale: float, kv_map: Optional[torch.Tensor], accumulate: bool
+) -> AttnParams:
+    B, Sq, Hq, D = q.shape
+    Sk, Hkv = k.shape[1], k.shape[2]
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.shape[-1] > 1 and t.stride(-1) != 1:
+            raise ValueError(f"{name} must be contiguous along the head dimension")
+    p = AttnParams()
+    p.q, p.k, p.v, p.out = _ptr(q), _ptr(k), _ptr(v), _ptr(out)
+    p.lse = _ptr(lse)
+    p.q_pos, p.k_pos = _ptr(q_pos), _ptr(k_pos)
+    p.kv_map = _ptr(kv_map)
+    p.q_stride = _i64x3(q.stride(0), q.stride(1), q.stride(2))
+    p.k_stride = _i64x3(k.stride(0), k.stride(1), k.stride(2))
+    p.v_stride = _i64x3(v.stride(0), v.stride(1), v.stride(2))
+    p.o_stride = _i64x3(out.stride(0), out.stride(1), out.stride(2))
+    if lse is not None:
+        p.lse_stride = _i64x3(lse.stride(0), lse.stride(1), lse.stride(2))
+    p.qpos_stride = _i64x2(q_pos.stride(0), q_pos.stride(1))
+    p.kpos_stride = _i64x2(k_pos.stride(0), k_pos.stride(1))
+    p.B, p.Sq, p.Sk, p.Hq, p.Hkv, p.D = B, Sq, Sk, Hq, Hkv, D
+    p.scale = float(scale)
+    p.causal = int(bool(causal))
+    p.in_dtype = dtype_code(q.dtype)
+    p.out_dtype = dtype_code(out.dtype)
+    p.accumulate = int(bool(accumulate))
+    return p
+
+
+def kernel_kind(p: AttnParams) -> int:
+    return load().cea_attn_kernel_kind(ctypes.byref(p))
+
+
+def attn_fwd(p: AttnParams, device: torch.device, entry: str = "cea_attn_fwd") -> None:
+    """Run cea_attn_fwd (or cea_decode_splitkv) on the current stream with a fresh workspace."""
+    lib = load()
+    need = lib.cea_attn_workspace_size(ctypes.byref(p))
+    ws = None
+    if need:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), need
+    fn = getattr(lib, entry)
+    _check(fn(ctypes.byref(p), _stream_ptr(device)), entry)
+
+
+def merge(outs: Sequence[torch.Tensor], lses: Sequence[torch.Tensor], out: torch.Tensor, lse: Optional[torch.Tensor]):
+    """cea_merge over partials sharing one layout (at most MAX_MERGE of them)."""
+    n = len(outs)
+    o0, l0 = outs[0], lses[0]
+    p = MergeParams()
+    p.n = n
+    for i in range(n):
+        p.outs[i] = outs[i].data_ptr()
+        p.lses[i] = lses[i].data_ptr()
+    p.out = out.data_ptr()
+    p.lse = _ptr(lse)
+    p.part_o_stride = _i64x3(o0.stride(0), o0.stride(1), o0.stride(2))
+    p.part_lse_stride = _i64x3(l0.stride(0), l0.stride(1), l0.stride(2))
+    p.o_stride = _i64x3(out.stride(0), out.stride(1), out.stride(2))
+    if lse is not None:
+        p.lse_stride = _i64x3(lse.stride(0), lse.stride(1), lse.stride(2))
+    B, Sq, H, D = o0.shape
+    p.B, p.Sq, p.H, p.D = B, Sq, H, D
+    p.part_dtype = dtype_code(o0.dtype)
+    p.out_dtype = dtype_code(out.dtype)
+    _check(load().cea_merge(ctypes.byref(p), _stream_ptr(out.device)), "cea_merge")
+
+
+def copy_segments(segments, D: int, elem_bytes: int, device: torch.device, entry: str = "cea_ulysses_pack") -> None:
+    """Run cea_ulysses_pack / unpack over ``(src, dst, nb, ns, nh)`` tensor segments.
+
+    ``src`` and ``dst`` are 4-D ``[nb, ns, nh, D]`` tensor views (any strides on the first three dims).
+    """
+    lib = load()
+    fn = getattr(lib, entry)
+    for start in range(0, len(segments), MAX_SEGMENTS):
+        chunk = segments[start : start + MAX_SEGMENTS]
+        p = CopyParams()
+        p.n, p.D, p.elem_bytes = len(chunk), D, elem_bytes
+        for i, (src, dst) in enumerate(chunk):
+            s = p.seg[i]
+            s.src, s.dst = src.data_ptr(), dst.data_ptr()
+            s.src_stride = _i64x3(src.stride(0), src.stride(1), src.stride(2))
+            s.dst_stride = _i64x3(dst.stride(0), dst.stride(1), dst.stride(2))
+            s.nb, s.ns, s.nh = src.shape[0], src.shape[1], src.shape[2]
+        _check(fn(ctypes.byref(p), _stream_ptr(device)), entry)
+
+
+def device_status(clear: bool = True, device: Optional[torch.device] = None) -> int:
+    """Device-side error word (bounded waits that expired); synchronises the current stream."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    v = ctypes.c_int(0)
+    _check(load().cea_device_status(ctypes.byref(v), int(clear), _stream_ptr(dev)), "cea_device_status")
+    return v.value

@@ -1,0 +1,408 @@
+// Prefill attention with log-sum-exp on the 5th-generation tensor cores (sm_100a).
+//
+// One CTA computes a 128-query tile of one (batch, query head) against every
+// visible 128-key tile of its KV head:
+//   warp 4      TMA producer: Q once, then K and V tiles into an NSTAGE ring
+//   warp 5      MMA issuer (one thread): S = Q K^T into TMEM (double-buffered),
+//               O += P V into a TMEM accumulator; completion via tcgen05.commit
+//   warps 0-3   softmax: one thread per query row (= TMEM lane); reads S from
+//               TMEM, applies the position mask, keeps the running max/sum in
+//               fp32 (log2 domain), writes P (bf16/fp16) into shared memory in
+//               the 128B-swizzled K-major operand layout, rescales O in TMEM when
+//               the running max grows by more than 2^8, and finally normalises O,
+//               writes out/lse and (accumulate mode) merges into the stored result.
+//
+// Tile skipping and masking follow per-tile position statistics computed by
+// tile_stats_kernel, so any token layout (contiguous, zigzag, padded, uneven)
+// takes the same path: fully invisible tiles are never loaded, fully visible
+// ones skip the element mask.
+#pragma once
+
+#include "cea_common.cuh"
+
+namespace cea {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int NUM_THREADS = 192;
+constexpr int kSoftmaxWarps = 4;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only when the max grows by > 256x
+
+template <int D>
+struct Layout {
+  static constexpr int KBOX = D / 64;              // 64-element (128-byte) swizzle boxes along D
+  static constexpr int BOX = 128 * 128;            // 128 rows x 128 B
+  static constexpr int TILE = KBOX * BOX;          // one Q, K or V tile
+  static constexpr int NSTAGE = D == 128 ? 2 : 4;  // K/V ring depth
+  static constexpr int PTILE = 2 * BOX;            // P: 128 rows x 128 keys (16-bit)
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + TILE;
+  static constexpr int OFF_V = OFF_K + NSTAGE * TILE;
+  static constexpr int OFF_P = OFF_V + NSTAGE * TILE;
+  static constexpr int OFF_BAR = OFF_P + 2 * PTILE;
+  static constexpr int B_QFULL = 0;
+  static constexpr int B_KFULL = 1;
+  static constexpr int B_KEMPTY = B_KFULL + NSTAGE;
+  static constexpr int B_VFULL = B_KEMPTY + NSTAGE;
+  static constexpr int B_VEMPTY = B_VFULL + NSTAGE;
+  static constexpr int B_SFULL = B_VEMPTY + NSTAGE;  // x2
+  static constexpr int B_PFULL = B_SFULL + 2;        // x2
+  static constexpr int B_PVDONE = B_PFULL + 2;       // x2
+  static constexpr int NBAR = B_PVDONE + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // TMEM base address, abort flag
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int SMEM_ALLOC = BYTES + 1024;      // slack to align the base to 1024 B
+  static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+};
+
+struct Params {
+  const int64_t* q_pos;
+  const int64_t* k_pos;
+  int64_t qpos_sb, qpos_ss, kpos_sb, kpos_ss;
+  void* out;
+  int64_t o_sb, o_ss, o_sh;
+  float* lse;
+  int64_t l_sb, l_sh, l_ss;
+  const int32_t* kv_map;
+  const TileStat* qstat;  // [B][nqt]
+  const TileStat* kstat;  // [B][nkt]
+  int B, Sq, Sk, Hq, Hkv, group, nqt, nkt;
+  float scale_log2;
+  int causal, out_dtype, accumulate;
+};
+
+// warp-uniform bounded wait: every lane waits, the warp continues only if all succeeded
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
+  const bool ok = mbar_wait(bar, parity, abort, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <int D, bool kBF16>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using L = Layout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::OFF_BAR + 8 * i; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // an earlier CTA gave up on a pipeline wait: fail fast instead of timing out again
+  if (*reinterpret_cast<volatile int*>(&g_cea_status) != 0) return;
+
+  // block -> (q tile, batch, head): heads of one q tile are adjacent (shared K/V stay in L2),
+  // and the tiles with the most keys (last positions) start first
+  int idx = blockIdx.x;
+  const int h = idx % p.Hq;
+  idx /= p.Hq;
+  const int b = idx % p.B;
+  idx /= p.B;
+  const int qt = p.nqt - 1 - idx;
+  const int kvh = p.kv_map ? p.kv_map[h] : h / p.group;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(L::B_QFULL), 1);
+    for (int s = 0; s < L::NSTAGE; ++s) {
+      mbar_init(bar(L::B_KFULL + s), 1);
+      mbar_init(bar(L::B_KEMPTY + s), 1);
+      mbar_init(bar(L::B_VFULL + s), 1);
+      mbar_init(bar(L::B_VEMPTY + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(L::B_SFULL + s), 1);
+      mbar_init(bar(L::B_PFULL + s), kSoftmaxWarps * 32);
+      mbar_init(bar(L::B_PVDONE + s), 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const TileStat qs = p.qstat[b * p.nqt + qt];
+  const TileStat* kst = p.kstat + static_cast<size_t>(b) * p.nkt;
+  const bool causal = p.causal != 0;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(L::B_QFULL), L::TILE);
+#pragma unroll
+      for (int kb = 0; kb < L::KBOX; ++kb)
+        tma_load_4d(sbase + L::OFF_Q + kb * L::BOX, &tmQ, bar(L::B_QFULL), kb * 64, qt * BM, h, b);
+      int it = 0;
+      for (int kt = 0; kt < p.nkt; ++kt) {
+        if (classify(qs, kst[kt], causal) == kSkip) continue;
+        const int st = it % L::NSTAGE;
+        const uint32_t n = it / L::NSTAGE;
+        if (n > 0 && !mbar_wait(bar(L::B_KEMPTY + st), (n - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(bar(L::B_KFULL + st), L::TILE);
+#pragma unroll
+        for (int kb = 0; kb < L::KBOX; ++kb)
+          tma_load_4d(sbase + L::OFF_K + st * L::TILE + kb * L::BOX, &tmK, bar(L::B_KFULL + st), kb * 64, kt * BN,
+                      kvh, b);
+        if (n > 0 && !mbar_wait(bar(L::B_VEMPTY + st), (n - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(bar(L::B_VFULL + st), L::TILE);
+#pragma unroll
+        for (int kb = 0; kb < L::KBOX; ++kb)
+          tma_load_4d(sbase + L::OFF_V + st * L::TILE + kb * L::BOX, &tmV, bar(L::B_VFULL + st), kb * 64, kt * BN,
+                      kvh, b);
+        ++it;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescQK = idesc_f16(kBF16, false, BM, BN);
+      constexpr uint32_t kIdescPV = idesc_f16(kBF16, true, BM, D);
+      const uint32_t tO = tmem + 256;
+      bool ok = mbar_wait(bar(L::B_QFULL), 0, abort_flag, CEA_DEV_TIMEOUT_MMA);
+      // O += P(j) V(j): P from shared memory (K-major over keys), V MN-major (D contiguous)
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j % L::NSTAGE;
+        if (!mbar_wait(bar(L::B_PFULL + (j & 1)), (j >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(bar(L::B_VFULL + st), (j / L::NSTAGE) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t pbase = sbase + L::OFF_P + (j & 1) * L::PTILE;
+        const uint32_t vbase = sbase + L::OFF_V + st * L::TILE;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t a = sw128_desc(pbase + (kk >> 2) * L::BOX + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(vbase + kk * 16 * 128, L::BOX, 1024);
+          umma_ss(tO, a, bd, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(L::B_VEMPTY + st));
+        umma_commit(bar(L::B_PVDONE + (j & 1)));
+        return true;
+      };
+      int it = 0;
+      for (int kt = 0; ok && kt < p.nkt; ++kt) {
+        if (classify(qs, kst[kt], causal) == kSkip) continue;
+        const int st = it % L::NSTAGE;
+        if (!mbar_wait(bar(L::B_KFULL + st), (it / L::NSTAGE) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // S(it) = Q K^T into the TMEM buffer it&1 (free: softmax(it-2) handed over P(it-2))
+        const uint32_t tS = tmem + (it & 1) * BN;
+        const uint32_t kbase = sbase + L::OFF_K + st * L::TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
+          umma_ss(tS, sw128_desc(sbase + L::OFF_Q + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), kIdescQK,
+                  kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(L::B_SFULL + (it & 1)));
+        umma_commit(bar(L::B_KEMPTY + st));
+        if (it > 0 && !issue_pv(it - 1)) {
+          ok = false;
+          break;
+        }
+        ++it;
+      }
+      if (ok && it > 0) issue_pv(it - 1);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int row = threadIdx.x;  // TMEM lane == query row within the tile
+    const int q_row = qt * BM + row;
+    const bool row_in = q_row < p.Sq;
+    const long long qpos = row_in ? p.q_pos[b * p.qpos_sb + static_cast<int64_t>(q_row) * p.qpos_ss] : -1ll;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int64_t* kpos_b = p.k_pos + b * p.kpos_sb;
+    float m = -INFINITY;  // running max actually used as the exponent offset (log2 domain)
+    float l = 0.f;        // running sum of exp2(s - m)
+    int it = 0;
+    bool ok = true;
+    for (int kt = 0; kt < p.nkt; ++kt) {
+      const int cls = classify(qs, kst[kt], causal);
+      if (cls == kSkip) continue;
+      if (!warp_wait(bar(L::B_SFULL + (it & 1)), (it >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_ld32(tmem + (it & 1) * BN + c * 32 + lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+      tmem_wait_ld();
+
+      float tmax = -INFINITY;
+      if (cls == kMasked) {
+        const int kbase = kt * BN;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int key = kbase + j;
+          const long long kp = key < p.Sk ? kpos_b[static_cast<int64_t>(key) * p.kpos_ss] : -1ll;
+          const bool vis = kp >= 0 && (!causal || kp <= qpos);
+          const float v = vis ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
+          s[j] = __float_as_uint(v);
+          tmax = fmaxf(tmax, v);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const float v = __uint_as_float(s[j]) * p.scale_log2;
+          s[j] = __float_as_uint(v);
+          tmax = fmaxf(tmax, v);
+        }
+      }
+      const float m_new = fmaxf(m, tmax);
+      const bool rescale = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
+      float alpha = 1.f;
+      if (m == -INFINITY) {
+        m = m_new;  // first visible key of this row: O and l are still zero
+      } else if (rescale) {
+        alpha = fast_exp2(m - m_new);
+        l *= alpha;
+        m = m_new;
+      }
+      const float m_use = (m == -INFINITY) ? 0.f : m;
+
+      // P(it) goes into buffer it&1, last read by PV(it-2)
+      if (it >= 2 &&
+          !warp_wait(bar(L::B_PVDONE + (it & 1)), ((it - 2) >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = smem + L::OFF_P + (it & 1) * L::PTILE + row * 128;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_exp2(__uint_as_float(s[c * 8 + 2 * e]) - m_use);
+          const float p1 = fast_exp2(__uint_as_float(s[c * 8 + 2 * e + 1]) - m_use);
+          rowsum += p0 + p1;
+          w[e] = pack2(p0, p1, kBF16);
+        }
+        const int chunk = (c & 7) ^ (row & 7);
+        *reinterpret_cast<uint4*>(prow + (c >> 3) * L::BOX + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rowsum;
+
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O holds PV(0..it-1); wait for PV(it-1) before scaling it in place
+        if (!warp_wait(bar(L::B_PVDONE + ((it - 1) & 1)), ((it - 1) >> 1) & 1, abort_flag,
+                       CEA_DEV_TIMEOUT_SOFTMAX)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + 256 + c * 32 + lane_base, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tmem + 256 + c * 32 + lane_base, o);
+        }
+        tmem_wait_st();
+      }
+      fence_async_smem();  // P stores -> visible to the tensor-core (async) proxy
+      tc_fence_before();
+      mbar_arrive(bar(L::B_PFULL + (it & 1)));
+      ++it;
+    }
+
+    // --------------------------------------------------------------- epilogue
+    if (ok && it > 0) {
+      ok = warp_wait(bar(L::B_PVDONE + ((it - 1) & 1)), ((it - 1) >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
+      tc_fence_after();
+    }
+    if (ok && !(it == 0 && p.accumulate)) {
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float lse_row = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
+      float w_old = 0.f, w_new = 1.f, lse_out = lse_row;
+      float* lse_ptr = p.lse ? p.lse + b * p.l_sb + h * p.l_sh + static_cast<int64_t>(q_row) * p.l_ss : nullptr;
+      if (p.accumulate && row_in) {
+        const float lse_old = *lse_ptr;
+        const float mx = fmaxf(lse_old, lse_row);
+        if (mx == -INFINITY) {
+          lse_out = -INFINITY;
+          w_old = 0.f;
+          w_new = 0.f;
+        } else {
+          lse_out = mx + log1pf(expf(-fabsf(lse_old - lse_row)));
+          w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - lse_out);
+          w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - lse_out);
+        }
+      }
+      const float scale_new = inv_l * w_new;
+      const int64_t obase = b * p.o_sb + static_cast<int64_t>(q_row) * p.o_ss + h * p.o_sh;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (it > 0) {
+          tmem_ld32(tmem + 256 + c * 32 + lane_base, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (!row_in) continue;
+        if (p.out_dtype == CEA_F32) {
+          float* dst = reinterpret_cast<float*>(p.out) + obase + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 v = make_float4(__uint_as_float(o[e]) * scale_new, __uint_as_float(o[e + 1]) * scale_new,
+                                   __uint_as_float(o[e + 2]) * scale_new, __uint_as_float(o[e + 3]) * scale_new);
+            if (p.accumulate) {
+              const float4 old = *reinterpret_cast<const float4*>(dst + e);
+              v.x += old.x * w_old;
+              v.y += old.y * w_old;
+              v.z += old.z * w_old;
+              v.w += old.w * w_old;
+            }
+            *reinterpret_cast<float4*>(dst + e) = v;
+          }
+        } else {
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + obase + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 v;
+            v.x = pack2(__uint_as_float(o[e]) * scale_new, __uint_as_float(o[e + 1]) * scale_new, kBF16);
+            v.y = pack2(__uint_as_float(o[e + 2]) * scale_new, __uint_as_float(o[e + 3]) * scale_new, kBF16);
+            v.z = pack2(__uint_as_float(o[e + 4]) * scale_new, __uint_as_float(o[e + 5]) * scale_new, kBF16);
+            v.w = pack2(__uint_as_float(o[e + 6]) * scale_new, __uint_as_float(o[e + 7]) * scale_new, kBF16);
+            *reinterpret_cast<uint4*>(dst + e) = v;
+          }
+        }
+      }
+      if (row_in && lse_ptr) *lse_ptr = lse_out;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace tc
+}  // namespace cea

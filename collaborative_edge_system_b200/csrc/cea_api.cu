@@ -1,0 +1,576 @@
+// C ABI of libcea.so: argument checking, kernel selection, TMA descriptors, launches.
+//
+// Everything is stream-ordered; no entry point synchronises the host (except
+// cea_device_status, which exists to do exactly that) or allocates memory.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "attn_simt.cuh"
+#include "attn_tc.cuh"
+#include "cea_common.cuh"
+#include "decode.cuh"
+
+using namespace cea;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_check(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CEA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return CEA_OK;
+}
+
+// ---------------------------------------------------------------- TMA maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [B, S, H, D] 16-bit tensor (D contiguous) as a 4-D tensor map with a (64, rows, 1, 1) box, 128B swizzle
+bool make_map(CUtensorMap* map, int dtype, const void* ptr, int D, int S, int H, int B, int64_t ss, int64_t sh,
+              int64_t sb, int rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return false;
+  // strides of size-1 dimensions are never used: give them any legal value
+  if (H == 1) sh = ss;
+  if (B == 1) sb = ss;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ss) * 2, static_cast<cuuint64_t>(sh) * 2,
+                                 static_cast<cuuint64_t>(sb) * 2};
+  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType t =
+      dtype == CEA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, t, 4, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// a [B, S, H, D] 16-bit operand TMA can read: 16-byte aligned base, strides multiples of 8 elements
+bool tma_ok(const void* ptr, const int64_t* st, int S, int H, int B) {
+  if (!aligned16(ptr)) return false;
+  const int64_t ss = st[1], sh = H == 1 ? st[1] : st[2], sb = B == 1 ? st[1] : st[0];
+  for (int64_t s : {ss, sh, sb})
+    if (s <= 0 || (s % 8) != 0 || s * 2 >= (int64_t(1) << 40)) return false;
+  (void)S;
+  return true;
+}
+
+int elem_bytes(int dt) { return dt == CEA_F64 ? 8 : (dt == CEA_F32 ? 4 : 2); }
+
+int num_sms() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+int validate(const cea_attn_params* p) {
+  if (p == nullptr) return fail(CEA_ERR_INVALID, "null params");
+  if (p->B < 0 || p->Sq < 0 || p->Sk < 0 || p->Hq < 0 || p->Hkv < 1 || p->D < 1)
+    return fail(CEA_ERR_INVALID, "invalid sizes B=%d Sq=%d Sk=%d Hq=%d Hkv=%d D=%d", p->B, p->Sq, p->Sk, p->Hq, p->Hkv,
+                p->D);
+  if (p->kv_map == nullptr && p->Hq % p->Hkv != 0)
+    return fail(CEA_ERR_INVALID, "%d query heads cannot share %d KV heads evenly", p->Hq, p->Hkv);
+  const int in = p->in_dtype, out = p->out_dtype;
+  if (in < CEA_F32 || in > CEA_F64) return fail(CEA_ERR_INVALID, "unknown input dtype %d", in);
+  const bool out_ok = in == CEA_F64 ? (out == CEA_F64) : (out == CEA_F32 || out == in);
+  if (!out_ok) return fail(CEA_ERR_UNSUPPORTED, "output dtype %d not available for input dtype %d", out, in);
+  if (p->accumulate && (p->lse == nullptr || (out != CEA_F32 && out != CEA_F64)))
+    return fail(CEA_ERR_INVALID, "accumulate needs lse and an fp32/fp64 output");
+  const bool empty = p->B == 0 || p->Sq == 0 || p->Hq == 0;
+  if (!empty && (p->out == nullptr || p->q_pos == nullptr || p->q == nullptr))
+    return fail(CEA_ERR_INVALID, "null q, out or q_pos");
+  if (!empty && p->Sk > 0 && (p->k == nullptr || p->v == nullptr || p->k_pos == nullptr))
+    return fail(CEA_ERR_INVALID, "null k, v or k_pos");
+  return CEA_OK;
+}
+
+enum Kind { kNone = 0, kTc = 1, kDecode = 2, kSimt = 3 };
+
+bool decode_ok(const cea_attn_params* p) {
+  if (p->in_dtype != CEA_BF16 && p->in_dtype != CEA_F16) return false;
+  if (p->D != 64 && p->D != 128) return false;
+  if (p->kv_map != nullptr) return false;
+  const int G = p->Hq / p->Hkv;
+  if (static_cast<int64_t>(p->Sq) * G > dec::MAX_ROWS) return false;
+  if ((reinterpret_cast<uintptr_t>(p->q) & 3u) != 0 || (p->q_stride[0] | p->q_stride[1] | p->q_stride[2]) & 1) return false;
+  return tma_ok(p->k, p->k_stride, p->Sk, p->Hkv, p->B) && tma_ok(p->v, p->v_stride, p->Sk, p->Hkv, p->B);
+}
+
+bool tc_ok(const cea_attn_params* p) {
+  if (p->in_dtype != CEA_BF16 && p->in_dtype != CEA_F16) return false;
+  if (p->D != 64 && p->D != 128) return false;
+  if (!tma_ok(p->q, p->q_stride, p->Sq, p->Hq, p->B) || !tma_ok(p->k, p->k_stride, p->Sk, p->Hkv, p->B) ||
+      !tma_ok(p->v, p->v_stride, p->Sk, p->Hkv, p->B))
+    return false;
+  // the epilogue stores 16-byte vectors of a row
+  const int vec = p->out_dtype == CEA_F32 ? 4 : 8;
+  if (!aligned16(p->out)) return false;
+  for (int i = 0; i < 3; ++i)
+    if (p->o_stride[i] % vec) return false;
+  return true;
+}
+
+int select_kind(const cea_attn_params* p) {
+  if (p->B == 0 || p->Sq == 0 || p->Hq == 0 || p->Sk == 0) return kNone;
+  if (decode_ok(p)) return kDecode;
+  if (tc_ok(p)) return kTc;
+  return kSimt;
+}
+
+// ---------------------------------------------------------------- decode sizing
+struct DecodePlan {
+  int nsplit, tiles_per_split;
+  size_t part_bytes;
+};
+
+DecodePlan decode_plan(const cea_attn_params* p) {
+  const int nkt = (p->Sk + dec::BKEYS - 1) / dec::BKEYS;
+  const int per_sm = p->D == 128 ? 2 : 3;  // resident CTAs per SM (shared-memory bound)
+  const int slots = num_sms() * per_sm;
+  const int64_t pairs = static_cast<int64_t>(p->B) * p->Hkv;
+  // pick the split count minimising (waves x tiles per split), preferring fewer splits on ties
+  int best = 1;
+  double best_cost = 1e30;
+  const int max_split = std::max(1, std::min(256, nkt));
+  for (int ns = 1; ns <= max_split; ++ns) {
+    const int tps = (nkt + ns - 1) / ns;
+    const int used = (nkt + tps - 1) / tps;
+    if (used != ns) continue;  // this split count leaves empty splits
+    const int64_t ctas = pairs * ns;
+    const double waves = static_cast<double>((ctas + slots - 1) / slots);
+    const double cost = waves * (tps + 2.0);  // +2: per-CTA pipeline fill and merge
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = ns;
+    }
+  }
+  DecodePlan plan;
+  plan.nsplit = best;
+  plan.tiles_per_split = (nkt + best - 1) / best;
+  const int64_t rows = static_cast<int64_t>(p->B) * p->Hq * p->Sq * best;
+  plan.part_bytes = static_cast<size_t>(rows) * (p->D + 1) * sizeof(float);
+  return plan;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t tc_stats_bytes(const cea_attn_params* p) {
+  const int nqt = (p->Sq + tc::BM - 1) / tc::BM, nkt = (p->Sk + tc::BN - 1) / tc::BN;
+  return align256(static_cast<size_t>(p->B) * (nqt + nkt) * sizeof(TileStat));
+}
+
+template <typename K>
+void allow_smem(K kernel, int bytes) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+// ---------------------------------------------------------------- launches
+int launch_empty(const cea_attn_params* p, cudaStream_t s) {
+  const int64_t rows = static_cast<int64_t>(p->B) * p->Sq * p->Hq;
+  const int grid = static_cast<int>(std::min<int64_t>(rows, 65535));
+  const int out_b = elem_bytes(p->out_dtype);
+#define CEA_FILL(UO, LT)                                                                                         \
+  fill_empty_kernel<UO, LT><<<grid, 64, 0, s>>>(reinterpret_cast<UO*>(p->out), p->o_stride[0], p->o_stride[1],    \
+                                                p->o_stride[2], reinterpret_cast<LT*>(p->lse), p->lse_stride[0], \
+                                                p->lse_stride[1], p->lse_stride[2], p->B, p->Sq, p->Hq, p->D)
+  if (p->in_dtype == CEA_F64) {
+    CEA_FILL(uint64_t, double);
+  } else if (out_b == 4) {
+    CEA_FILL(uint32_t, float);
+  } else {
+    CEA_FILL(uint16_t, float);
+  }
+#undef CEA_FILL
+  return cuda_check("fill_empty_kernel");
+}
+
+int launch_tc(const cea_attn_params* p, cudaStream_t s) {
+  const size_t need = tc_stats_bytes(p);
+  if (p->workspace == nullptr || p->workspace_bytes < need)
+    return fail(CEA_ERR_WORKSPACE, "tcgen05 attention needs %zu workspace bytes, got %zu", need, p->workspace_bytes);
+  const int nqt = (p->Sq + tc::BM - 1) / tc::BM, nkt = (p->Sk + tc::BN - 1) / tc::BN;
+  TileStat* qstat = reinterpret_cast<TileStat*>(p->workspace);
+  TileStat* kstat = qstat + static_cast<size_t>(p->B) * nqt;
+  {
+    const int warps = p->B * (nqt + nkt);
+    (void)warps;
+    const int wq = p->B * nqt, wk = p->B * nkt;
+    tile_stats_kernel<<<(wq + 3) / 4, 128, 0, s>>>(p->q_pos, p->qpos_stride[0], p->qpos_stride[1], p->Sq, nqt, p->B,
+                                                   0, qstat);
+    tile_stats_kernel<<<(wk + 3) / 4, 128, 0, s>>>(p->k_pos, p->kpos_stride[0], p->kpos_stride[1], p->Sk, nkt, p->B,
+                                                   1, kstat);
+    if (int e = cuda_check("tile_stats_kernel")) return e;
+  }
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, p->in_dtype, p->q, p->D, p->Sq, p->Hq, p->B, p->q_stride[1], p->q_stride[2], p->q_stride[0], 128) ||
+      !make_map(&mk, p->in_dtype, p->k, p->D, p->Sk, p->Hkv, p->B, p->k_stride[1], p->k_stride[2], p->k_stride[0], 128) ||
+      !make_map(&mv, p->in_dtype, p->v, p->D, p->Sk, p->Hkv, p->B, p->v_stride[1], p->v_stride[2], p->v_stride[0], 128))
+    return fail(CEA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the attention operands");
+  tc::Params tp;
+  tp.q_pos = p->q_pos;
+  tp.k_pos = p->k_pos;
+  tp.qpos_sb = p->qpos_stride[0];
+  tp.qpos_ss = p->qpos_stride[1];
+  tp.kpos_sb = p->kpos_stride[0];
+  tp.kpos_ss = p->kpos_stride[1];
+  tp.out = p->out;
+  tp.o_sb = p->o_stride[0];
+  tp.o_ss = p->o_stride[1];
+  tp.o_sh = p->o_stride[2];
+  tp.lse = reinterpret_cast<float*>(p->lse);
+  tp.l_sb = p->lse_stride[0];
+  tp.l_sh = p->lse_stride[1];
+  tp.l_ss = p->lse_stride[2];
+  tp.kv_map = p->kv_map;
+  tp.qstat = qstat;
+  tp.kstat = kstat;
+  tp.B = p->B;
+  tp.Sq = p->Sq;
+  tp.Sk = p->Sk;
+  tp.Hq = p->Hq;
+  tp.Hkv = p->Hkv;
+  tp.group = p->kv_map ? 1 : p->Hq / p->Hkv;
+  tp.nqt = nqt;
+  tp.nkt = nkt;
+  tp.scale_log2 = static_cast<float>(p->scale * 1.4426950408889634);
+  tp.causal = p->causal;
+  tp.out_dtype = p->out_dtype;
+  tp.accumulate = p->accumulate;
+  const int64_t grid = static_cast<int64_t>(nqt) * p->Hq * p->B;
+  if (grid > 0x7fffffff) return fail(CEA_ERR_UNSUPPORTED, "grid too large");
+#define CEA_TC(DD, BF)                                                                                       \
+  do {                                                                                                       \
+    auto k = tc::attn_fwd_tc_kernel<DD, BF>;                                                                 \
+    allow_smem(k, tc::Layout<DD>::SMEM_ALLOC);                                                               \
+    k<<<static_cast<unsigned>(grid), tc::NUM_THREADS, tc::Layout<DD>::SMEM_ALLOC, s>>>(mq, mk, mv, tp);      \
+  } while (0)
+  const bool bf = p->in_dtype == CEA_BF16;
+  if (p->D == 128) {
+    if (bf) CEA_TC(128, true); else CEA_TC(128, false);
+  } else {
+    if (bf) CEA_TC(64, true); else CEA_TC(64, false);
+  }
+#undef CEA_TC
+  return cuda_check("attn_fwd_tc_kernel");
+}
+
+int launch_decode(const cea_attn_params* p, cudaStream_t s) {
+  const DecodePlan plan = decode_plan(p);
+  if (p->workspace == nullptr || p->workspace_bytes < plan.part_bytes)
+    return fail(CEA_ERR_WORKSPACE, "split-KV decode needs %zu workspace bytes, got %zu", plan.part_bytes,
+                p->workspace_bytes);
+  CUtensorMap mk, mv;
+  if (!make_map(&mk, p->in_dtype, p->k, p->D, p->Sk, p->Hkv, p->B, p->k_stride[1], p->k_stride[2], p->k_stride[0],
+                dec::BKEYS) ||
+      !make_map(&mv, p->in_dtype, p->v, p->D, p->Sk, p->Hkv, p->B, p->v_stride[1], p->v_stride[2], p->v_stride[0],
+                dec::BKEYS))
+    return fail(CEA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
+  const int64_t rows = static_cast<int64_t>(p->B) * p->Hq * p->Sq;
+  dec::Params dp;
+  dp.q = p->q;
+  dp.q_sb = p->q_stride[0];
+  dp.q_ss = p->q_stride[1];
+  dp.q_sh = p->q_stride[2];
+  dp.q_pos = p->q_pos;
+  dp.qpos_sb = p->qpos_stride[0];
+  dp.qpos_ss = p->qpos_stride[1];
+  dp.k_pos = p->k_pos;
+  dp.kpos_sb = p->kpos_stride[0];
+  dp.kpos_ss = p->kpos_stride[1];
+  dp.part_o = reinterpret_cast<float*>(p->workspace);
+  dp.part_lse = dp.part_o + rows * plan.nsplit * p->D;
+  dp.B = p->B;
+  dp.Sq = p->Sq;
+  dp.Sk = p->Sk;
+  dp.Hq = p->Hq;
+  dp.Hkv = p->Hkv;
+  dp.G = p->Hq / p->Hkv;
+  dp.nsplit = plan.nsplit;
+  dp.tiles_per_split = plan.tiles_per_split;
+  dp.scale_log2 = static_cast<float>(p->scale * 1.4426950408889634);
+  dp.causal = p->causal;
+  const dim3 grid(plan.nsplit, p->Hkv, p->B);
+#define CEA_DEC(DD, BF)                                                                              \
+  do {                                                                                               \
+    auto k = dec::decode_partial_kernel<DD, BF>;                                                     \
+    allow_smem(k, dec::Layout<DD>::SMEM_ALLOC);                                                      \
+    k<<<grid, dec::NTHREADS, dec::Layout<DD>::SMEM_ALLOC, s>>>(mk, mv, dp);                          \
+  } while (0)
+  const bool bf = p->in_dtype == CEA_BF16;
+  if (p->D == 128) {
+    if (bf) CEA_DEC(128, true); else CEA_DEC(128, false);
+  } else {
+    if (bf) CEA_DEC(64, true); else CEA_DEC(64, false);
+  }
+#undef CEA_DEC
+  if (int e = cuda_check("decode_partial_kernel")) return e;
+  dec::CombineParams cp;
+  cp.part_o = dp.part_o;
+  cp.part_lse = dp.part_lse;
+  cp.out = p->out;
+  cp.lse = reinterpret_cast<float*>(p->lse);
+  cp.o_sb = p->o_stride[0];
+  cp.o_ss = p->o_stride[1];
+  cp.o_sh = p->o_stride[2];
+  cp.l_sb = p->lse_stride[0];
+  cp.l_sh = p->lse_stride[1];
+  cp.l_ss = p->lse_stride[2];
+  cp.B = p->B;
+  cp.Sq = p->Sq;
+  cp.Hq = p->Hq;
+  cp.D = p->D;
+  cp.nsplit = plan.nsplit;
+  cp.out_dtype = p->out_dtype;
+  cp.accumulate = p->accumulate;
+  const int64_t blocks = (rows * 32 + 255) / 256;
+  dec::decode_combine_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(cp);
+  return cuda_check("decode_combine_kernel");
+}
+
+template <typename T, typename A, typename O, int DMAX>
+void launch_simt_t(const simt::Params& sp, const cea_attn_params* p, cudaStream_t s) {
+  auto k = simt::attn_simt_kernel<T, A, O, DMAX>;
+  constexpr size_t bytes = simt::smem_bytes<A, DMAX>();
+  allow_smem(k, static_cast<int>(bytes));
+  const dim3 grid((p->Sq + simt::BQ - 1) / simt::BQ, p->Hq, p->B);
+  k<<<grid, simt::NT, bytes, s>>>(sp);
+}
+
+template <typename T, typename A, typename O>
+int launch_simt_d(const simt::Params& sp, const cea_attn_params* p, cudaStream_t s) {
+  if (p->D <= 32) launch_simt_t<T, A, O, 32>(sp, p, s);
+  else if (p->D <= 64) launch_simt_t<T, A, O, 64>(sp, p, s);
+  else if (p->D <= 128) launch_simt_t<T, A, O, 128>(sp, p, s);
+  else if (sizeof(A) == 4 && p->D <= 256) launch_simt_t<T, A, O, (sizeof(A) == 4 ? 256 : 128)>(sp, p, s);
+  else return fail(CEA_ERR_UNSUPPORTED, "head dim %d too large for the CUDA-core attention kernel", p->D);
+  return cuda_check("attn_simt_kernel");
+}
+
+int launch_simt(const cea_attn_params* p, cudaStream_t s) {
+  simt::Params sp;
+  sp.q = p->q;
+  sp.k = p->k;
+  sp.v = p->v;
+  sp.out = p->out;
+  sp.lse = p->lse;
+  sp.q_pos = p->q_pos;
+  sp.k_pos = p->k_pos;
+  sp.kv_map = p->kv_map;
+  sp.q_sb = p->q_stride[0];
+  sp.q_ss = p->q_stride[1];
+  sp.q_sh = p->q_stride[2];
+  sp.k_sb = p->k_stride[0];
+  sp.k_ss = p->k_stride[1];
+  sp.k_sh = p->k_stride[2];
+  sp.v_sb = p->v_stride[0];
+  sp.v_ss = p->v_stride[1];
+  sp.v_sh = p->v_stride[2];
+  sp.o_sb = p->o_stride[0];
+  sp.o_ss = p->o_stride[1];
+  sp.o_sh = p->o_stride[2];
+  sp.l_sb = p->lse_stride[0];
+  sp.l_sh = p->lse_stride[1];
+  sp.l_ss = p->lse_stride[2];
+  sp.qpos_sb = p->qpos_stride[0];
+  sp.qpos_ss = p->qpos_stride[1];
+  sp.kpos_sb = p->kpos_stride[0];
+  sp.kpos_ss = p->kpos_stride[1];
+  sp.B = p->B;
+  sp.Sq = p->Sq;
+  sp.Sk = p->Sk;
+  sp.Hq = p->Hq;
+  sp.Hkv = p->Hkv;
+  sp.D = p->D;
+  sp.group = p->kv_map ? 1 : p->Hq / p->Hkv;
+  sp.scale = p->scale;
+  sp.causal = p->causal;
+  sp.accumulate = p->accumulate;
+  switch (p->in_dtype) {
+    case CEA_F64:
+      return launch_simt_d<double, double, double>(sp, p, s);
+    case CEA_F32:
+      return launch_simt_d<float, float, float>(sp, p, s);
+    case CEA_BF16:
+      return p->out_dtype == CEA_F32 ? launch_simt_d<__nv_bfloat16, float, float>(sp, p, s)
+                                     : launch_simt_d<__nv_bfloat16, float, __nv_bfloat16>(sp, p, s);
+    case CEA_F16:
+      return p->out_dtype == CEA_F32 ? launch_simt_d<__half, float, float>(sp, p, s)
+                                     : launch_simt_d<__half, float, __half>(sp, p, s);
+  }
+  return fail(CEA_ERR_UNSUPPORTED, "dtype");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* cea_last_error(void) { return g_last_error.c_str(); }
+
+int cea_abi_version(void) { return CEA_ABI_VERSION; }
+
+int cea_attn_kernel_kind(const cea_attn_params* p) {
+  if (validate(p) != CEA_OK) return -1;
+  return select_kind(p);
+}
+
+size_t cea_attn_workspace_size(const cea_attn_params* p) {
+  if (validate(p) != CEA_OK) return 0;
+  switch (select_kind(p)) {
+    case kTc:
+      return tc_stats_bytes(p);
+    case kDecode:
+      return align256(decode_plan(p).part_bytes);
+    default:
+      return 0;
+  }
+}
+
+int cea_attn_fwd(const cea_attn_params* p, void* stream) {
+  if (int e = validate(p)) return e;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (p->B == 0 || p->Sq == 0 || p->Hq == 0) return CEA_OK;
+  if (p->Sk == 0) return p->accumulate ? CEA_OK : launch_empty(p, s);
+  switch (select_kind(p)) {
+    case kDecode:
+      return launch_decode(p, s);
+    case kTc:
+      return launch_tc(p, s);
+    default:
+      return launch_simt(p, s);
+  }
+}
+
+int cea_decode_splitkv(const cea_attn_params* p, void* stream) {
+  if (int e = validate(p)) return e;
+  if (p->B == 0 || p->Sq == 0 || p->Hq == 0) return CEA_OK;
+  if (p->Sk == 0) return p->accumulate ? CEA_OK : launch_empty(p, reinterpret_cast<cudaStream_t>(stream));
+  if (!decode_ok(p))
+    return fail(CEA_ERR_UNSUPPORTED,
+                "split-KV decode needs bf16/f16, D in {64,128}, uniform GQA, Sq*group <= 16 and TMA-aligned K/V");
+  return launch_decode(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cea_merge(const cea_merge_params* p, void* stream) {
+  if (p == nullptr || p->n < 1 || p->n > CEA_MAX_MERGE) return fail(CEA_ERR_INVALID, "merge needs 1..%d partials", CEA_MAX_MERGE);
+  if (p->B < 0 || p->Sq < 0 || p->H < 0 || p->D < 1) return fail(CEA_ERR_INVALID, "invalid merge sizes");
+  if (p->out == nullptr) return fail(CEA_ERR_INVALID, "null merge output");
+  for (int i = 0; i < p->n; ++i)
+    if (p->outs[i] == nullptr || p->lses[i] == nullptr) return fail(CEA_ERR_INVALID, "null partial %d", i);
+  const int64_t rows = static_cast<int64_t>(p->B) * p->Sq * p->H;
+  if (rows == 0) return CEA_OK;
+  MergeArgs a;
+  a.n = p->n;
+  for (int i = 0; i < p->n; ++i) {
+    a.outs[i] = p->outs[i];
+    a.lses[i] = p->lses[i];
+  }
+  a.out = p->out;
+  a.lse = p->lse;
+  a.po_sb = p->part_o_stride[0];
+  a.po_ss = p->part_o_stride[1];
+  a.po_sh = p->part_o_stride[2];
+  a.pl_sb = p->part_lse_stride[0];
+  a.pl_sh = p->part_lse_stride[1];
+  a.pl_ss = p->part_lse_stride[2];
+  a.o_sb = p->o_stride[0];
+  a.o_ss = p->o_stride[1];
+  a.o_sh = p->o_stride[2];
+  a.l_sb = p->lse_stride[0];
+  a.l_sh = p->lse_stride[1];
+  a.l_ss = p->lse_stride[2];
+  a.B = p->B;
+  a.Sq = p->Sq;
+  a.H = p->H;
+  a.D = p->D;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = static_cast<unsigned>((rows * 32 + 255) / 256);
+  if (p->part_dtype == CEA_F32) {
+    if (p->out_dtype == CEA_F32) merge_kernel<float, float><<<blocks, 256, 0, s>>>(a);
+    else if (p->out_dtype == CEA_BF16) merge_kernel<float, __nv_bfloat16><<<blocks, 256, 0, s>>>(a);
+    else if (p->out_dtype == CEA_F16) merge_kernel<float, __half><<<blocks, 256, 0, s>>>(a);
+    else return fail(CEA_ERR_UNSUPPORTED, "merge output dtype %d for fp32 partials", p->out_dtype);
+  } else if (p->part_dtype == CEA_F64) {
+    if (p->out_dtype == CEA_F64) merge_kernel<double, double><<<blocks, 256, 0, s>>>(a);
+    else if (p->out_dtype == CEA_F32) merge_kernel<double, float><<<blocks, 256, 0, s>>>(a);
+    else return fail(CEA_ERR_UNSUPPORTED, "merge output dtype %d for fp64 partials", p->out_dtype);
+  } else {
+    return fail(CEA_ERR_UNSUPPORTED, "merge partial dtype %d", p->part_dtype);
+  }
+  return cuda_check("merge_kernel");
+}
+
+static int copy_segments(const cea_copy_params* p, void* stream, const char* what) {
+  if (p == nullptr || p->n < 0 || p->n > CEA_MAX_SEGMENTS) return fail(CEA_ERR_INVALID, "%s: 0..%d segments", what, CEA_MAX_SEGMENTS);
+  if (p->elem_bytes != 2 && p->elem_bytes != 4 && p->elem_bytes != 8) return fail(CEA_ERR_INVALID, "%s: element size", what);
+  if (p->D < 1) return fail(CEA_ERR_INVALID, "%s: D", what);
+  CopyArgs a;
+  a.n = p->n;
+  a.D = p->D;
+  a.elem_bytes = p->elem_bytes;
+  bool vec = (static_cast<int64_t>(p->D) * p->elem_bytes) % 16 == 0;
+  int64_t most = 0;
+  for (int i = 0; i < p->n; ++i) {
+    const cea_segment& sg = p->seg[i];
+    if (sg.nb < 0 || sg.ns < 0 || sg.nh < 0) return fail(CEA_ERR_INVALID, "%s: segment %d sizes", what, i);
+    const int64_t rows = static_cast<int64_t>(sg.nb) * sg.ns * sg.nh;
+    if (rows > 0 && (sg.src == nullptr || sg.dst == nullptr)) return fail(CEA_ERR_INVALID, "%s: null segment %d", what, i);
+    most = std::max(most, rows);
+    vec = vec && aligned16(sg.src) && aligned16(sg.dst);
+    for (int j = 0; j < 3; ++j)
+      vec = vec && (sg.src_stride[j] * p->elem_bytes) % 16 == 0 && (sg.dst_stride[j] * p->elem_bytes) % 16 == 0;
+    a.seg[i] = sg;
+  }
+  a.vec = vec ? 1 : 0;
+  if (p->n == 0 || most == 0) return CEA_OK;
+  const int64_t units = vec ? (static_cast<int64_t>(p->D) * p->elem_bytes / 16) : p->D;
+  const int64_t blocks = std::min<int64_t>((most * units + 255) / 256, 4 * 148 * 4);
+  copy_segments_kernel<<<dim3(static_cast<unsigned>(blocks), p->n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return cuda_check(what);
+}
+
+int cea_ulysses_pack(const cea_copy_params* p, void* stream) { return copy_segments(p, stream, "cea_ulysses_pack"); }
+int cea_ulysses_unpack(const cea_copy_params* p, void* stream) { return copy_segments(p, stream, "cea_ulysses_unpack"); }
+
+int cea_device_status(int* status_out, int clear, void* stream) {
+  if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return cuda_check("cea_device_status");
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_cea_status, sizeof(int)) != cudaSuccess) return cuda_check("cea_device_status");
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_cea_status, &zero, sizeof(int)) != cudaSuccess) return cuda_check("cea_device_status");
+  }
+  if (status_out) *status_out = v;
+  return CEA_OK;
+}
+
+}  // extern "C"

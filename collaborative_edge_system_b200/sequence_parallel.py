@@ -1,0 +1,288 @@
+"""Sequence-parallel attention across GPUs: ring, Ulysses and distributed-KV decode.
+
+Drop-in for collab_infer ``parallel/sequence_parallel.py`` (same signatures,
+uneven per-rank sizes, any token layout, GQA/MQA head shards).  What changes
+is where the work runs:
+
+* ``ring_attention``: step t sends the current K||V block (and positions) to
+  rank r+1 and receives the next from r-1 in one grouped NCCL operation on
+  NCCL's stream, while the attention kernel runs on the compute stream and
+  merges its result into the running (out, lse) in its epilogue - the
+  reference's separate ``merge_attention`` pass disappears.  Invisible tiles
+  (the causal future, padding) are skipped on the device, so unlike the
+  reference (``sequence_parallel.py:117``) no step synchronises the host.
+* ``ulysses_scatter`` / ``ulysses_gather``: per-peer head slices are packed
+  into one send buffer by a copy kernel (no per-peer ``torch.cat``), moved by
+  a single uneven all-to-all, and attention reads the received q/k/v as
+  strided views.
+* ``distributed_kv_attention``: the split-KV decode kernel on the local cache
+  shard, an all-gather of the packed ``[B, Sq, H, D+1]`` partials and an
+  n-way merge kernel that writes ``q.dtype`` directly.
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from .attention import KVMap, accumulation_dtype, attend_into, attention, attention_with_lse, _merge
+from .comm import Communicator
+from .partition import HeadShard, SequenceLayout, offsets_of
+
+TAG_RING_KV = 21
+TAG_RING_POS = 22
+
+
+def _copy_segments(pairs: List[Tuple[torch.Tensor, torch.Tensor]]) -> None:
+    """Copy each ``src`` view into its ``dst`` view ([nb, ns, nh, D] each) with one kernel launch."""
+    if not pairs:
+        return
+    src0 = pairs[0][0]
+    _lib.copy_segments(pairs, src0.shape[-1], src0.element_size(), src0.device, "cea_ulysses_pack")
+
+
+def shard_sequence(x: torch.Tensor, layout: SequenceLayout, rank: int, dim: int = 1) -> torch.Tensor:
+    """This rank's tokens of a full-sequence tensor (``sequence_parallel.py:50-52``)."""
+    return layout.shard(x, rank, dim)
+
+
+def gather_sequence(x_local: torch.Tensor, layout: SequenceLayout, comm: Communicator, dim: int = 1) -> torch.Tensor:
+    """All-gather sequence shards in global token order (``sequence_parallel.py:55-62``)."""
+    if comm.size == 1:
+        return x_local
+    return layout.unshard(comm.all_gather_list(x_local, dim=dim, sizes=layout.sizes), dim=dim)
+
+
+# ----------------------------------------------------------------------------
+# ring attention
+# ----------------------------------------------------------------------------
+def ring_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    q_pos: torch.Tensor,
+    k_pos: torch.Tensor,
+    comm: Communicator,
+    kv_sizes: Sequence[int],
+    *,
+    causal: bool = True,
+    scale: Optional[float] = None,
+    kv_map: KVMap = None,
+    kv_block: Optional[int] = None,
+    return_lse: bool = False,
+):
+    """Local queries against the keys/values of every rank (``sequence_parallel.py:68-130``).
+
+    At step t rank i computes on the block that originated at rank i-t while
+    that block travels on to i+1.  Returns ``[B, s_i, Hq, D]`` in ``q.dtype``;
+    with ``return_lse=True`` also the ``[B, Hq, s_i]`` log-sum-exp over all
+    keys (accumulation dtype), which the reference computes but drops.
+    """
+    n, r = comm.size, comm.rank
+    if n == 1:
+        out, lse = attention_with_lse(q, k, v, q_pos, k_pos, causal=causal, scale=scale, kv_map=kv_map,
+                                      kv_block=kv_block)
+        res = out.to(q.dtype)
+        return (res, lse) if return_lse else res
+    if len(kv_sizes) != n or kv_sizes[r] != k.shape[1]:
+        raise ValueError(f"kv_sizes {list(kv_sizes)} inconsistent with local block of {k.shape[1]} tokens")
+    B, Sq, Hq, D = q.shape
+    Hkv = k.shape[2]
+    acc = accumulation_dtype(q.dtype)
+    out = torch.empty(B, Sq, Hq, D, dtype=acc, device=q.device)
+    lse = torch.empty(B, Hq, Sq, dtype=acc, device=q.device)
+    # K and V travel as one message (optionally narrower); received blocks are forwarded as they arrive
+    wire = comm.to_wire(torch.stack([k, v])).contiguous()
+    k_cur, v_cur = k, v
+    pos = k_pos.to(device=q.device, dtype=torch.int64).contiguous()
+    nxt, prv = (r + 1) % n, (r - 1) % n
+    for step in range(n):
+        pending = None
+        if step < n - 1:
+            src = (r - step - 1) % n
+            pending = comm.ring_exchange(
+                [wire, pos], nxt, [((2, B, kv_sizes[src], Hkv, D), wire.dtype), ((B, kv_sizes[src]), torch.int64)],
+                prv)
+        attend_into(q, k_cur, v_cur, q_pos, pos, out, lse, causal=causal, scale=scale, kv_map=kv_map,
+                    accumulate=step > 0)
+        if pending is not None:
+            wire, pos = pending.wait()
+            k_cur, v_cur = wire[0].to(k.dtype), wire[1].to(k.dtype)
+    res = out.to(q.dtype)
+    return (res, lse) if return_lse else res
+
+
+# ----------------------------------------------------------------------------
+# Ulysses (all-to-all) attention
+# ----------------------------------------------------------------------------
+def _check_ulysses(comm: Communicator, seq_sizes: Sequence[int], head_shards: Sequence[HeadShard], s_local: int):
+    if len(seq_sizes) != comm.size or seq_sizes[comm.rank] != s_local:
+        raise ValueError(f"seq_sizes {list(seq_sizes)} inconsistent with local shard of {s_local} tokens")
+    if len(head_shards) != comm.size:
+        raise ValueError("need one head shard per rank")
+
+
+def ulysses_scatter(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    positions: torch.Tensor,
+    comm: Communicator,
+    seq_sizes: Sequence[int],
+    head_shards: Sequence[HeadShard],
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Sequence-sharded ``[B, s_i, H, D]`` -> this rank's heads over all tokens (``:143-179``).
+
+    Returns ``(q, k, v, positions)`` over the full sequence (rank order);
+    q/k/v are views of one received buffer.
+    """
+    n, r = comm.size, comm.rank
+    B, s_local, _, D = q.shape
+    _check_ulysses(comm, seq_sizes, head_shards, s_local)
+    me = head_shards[r]
+    widths = [sh.q_count + 2 * sh.kv_count for sh in head_shards]
+    counts = [B * s_local * w * D for w in widths]
+    send = torch.empty(sum(counts), dtype=q.dtype, device=q.device)
+    pairs = []
+    for sh, off, w in zip(head_shards, offsets_of(counts), widths):
+        blk = send[off : off + B * s_local * w * D].view(B, s_local, w, D)
+        pairs.append((q[:, :, sh.q_start : sh.q_start + sh.q_count], blk[:, :, : sh.q_count]))
+        pairs.append((k[:, :, sh.kv_start : sh.kv_start + sh.kv_count], blk[:, :, sh.q_count : sh.q_count + sh.kv_count]))
+        pairs.append((v[:, :, sh.kv_start : sh.kv_start + sh.kv_count], blk[:, :, sh.q_count + sh.kv_count :]))
+    _copy_segments(pairs)
+    w_me = widths[r]
+    S = sum(seq_sizes)
+    wire_send = comm.to_wire(send)
+    recv_counts = [B * s * w_me * D for s in seq_sizes]
+    recv = torch.empty(sum(recv_counts), dtype=wire_send.dtype, device=q.device)
+    comm.all_to_all_single(recv, wire_send, recv_counts, counts).wait()
+    if recv.dtype != q.dtype:
+        recv = recv.to(q.dtype)
+    if B == 1:
+        full = recv.view(1, S, w_me, D)  # per-rank blocks are already in token order
+    else:
+        full = torch.empty(B, S, w_me, D, dtype=q.dtype, device=q.device)
+        _copy_segments([
+            (recv[off : off + c].view(B, s, w_me, D), full[:, t0 : t0 + s])
+            for off, c, s, t0 in zip(offsets_of(recv_counts), recv_counts, seq_sizes, offsets_of(seq_sizes))
+        ])
+    q_f, k_f, v_f = full.split([me.q_count, me.kv_count, me.kv_count], dim=2)
+    pos_f = comm.all_gather(positions, dim=1, sizes=seq_sizes)
+    return q_f, k_f, v_f, pos_f
+
+
+def ulysses_gather(
+    out_heads: torch.Tensor, comm: Communicator, seq_sizes: Sequence[int], head_shards: Sequence[HeadShard]
+) -> torch.Tensor:
+    """Head-sharded ``[B, S, h_i, D]`` -> ``[B, s_i, H, D]`` (``sequence_parallel.py:182-194``)."""
+    n, r = comm.size, comm.rank
+    B, S, h_r, D = out_heads.shape
+    starts = offsets_of(seq_sizes)
+    counts = [B * s * h_r * D for s in seq_sizes]
+    if B == 1 and out_heads.is_contiguous():
+        send = out_heads.reshape(-1)  # token blocks of [1, S, h, D] are already rank-major
+    else:
+        send = torch.empty(sum(counts), dtype=out_heads.dtype, device=out_heads.device)
+        _copy_segments([
+            (out_heads[:, t0 : t0 + s], send[off : off + c].view(B, s, h_r, D))
+            for t0, s, off, c in zip(starts, seq_sizes, offsets_of(counts), counts)
+        ])
+    s_r = seq_sizes[r]
+    q_counts = [sh.q_count for sh in head_shards]
+    recv_counts = [B * s_r * qc * D for qc in q_counts]
+    wire_send = comm.to_wire(send)
+    recv = torch.empty(sum(recv_counts), dtype=wire_send.dtype, device=out_heads.device)
+    comm.all_to_all_single(recv, wire_send, recv_counts, counts).wait()
+    if recv.dtype != out_heads.dtype:
+        recv = recv.to(out_heads.dtype)
+    Hq = sum(q_counts)
+    out = torch.empty(B, s_r, Hq, D, dtype=out_heads.dtype, device=out_heads.device)
+    _copy_segments([
+        (recv[off : off + c].view(B, s_r, qc, D), out[:, :, sh.q_start : sh.q_start + qc])
+        for off, c, qc, sh in zip(offsets_of(recv_counts), recv_counts, q_counts, head_shards)
+    ])
+    return out
+
+
+def ulysses_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    positions: torch.Tensor,
+    comm: Communicator,
+    seq_sizes: Sequence[int],
+    head_shards: Sequence[HeadShard],
+    *,
+    causal: bool = True,
+    scale: Optional[float] = None,
+    past: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+    kv_block: Optional[int] = None,
+) -> Tuple[torch.Tensor, Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+    """All-to-all sequence parallel attention (``sequence_parallel.py:197-239``).
+
+    Returns ``(out [B, s_i, Hq, D], (k_heads, v_heads, pos_full))``; the second
+    element holds this rank's KV heads over the new tokens, for a head-sharded cache.
+    """
+    me = head_shards[comm.rank]
+    q_f, k_f, v_f, pos_f = ulysses_scatter(q, k, v, positions, comm, seq_sizes, head_shards)
+    k_att, v_att, p_att = k_f, v_f, pos_f
+    if past is not None and past[0].shape[1] > 0:
+        k_att = torch.cat([past[0], k_f], dim=1)
+        v_att = torch.cat([past[1], v_f], dim=1)
+        p_att = torch.cat([past[2].to(pos_f.device), pos_f], dim=1)
+    o = attention(q_f, k_att, v_att, pos_f, p_att, causal=causal, scale=scale, kv_map=me.kv_map, kv_block=kv_block)
+    out = ulysses_gather(o, comm, seq_sizes, head_shards)
+    return out, (k_f.contiguous(), v_f.contiguous(), pos_f)
+
+
+def gather_heads(out_local: torch.Tensor, comm: Communicator, head_shards: Sequence[HeadShard]) -> torch.Tensor:
+    """All-gather per-rank head slices ``[B, S, h_i, D]`` into ``[B, S, H, D]`` (``:242-244``)."""
+    return comm.all_gather(out_local, dim=2, sizes=[sh.q_count for sh in head_shards])
+
+
+# ----------------------------------------------------------------------------
+# decoding against a distributed KV cache
+# ----------------------------------------------------------------------------
+def distributed_kv_attention(
+    q: torch.Tensor,
+    k_local: torch.Tensor,
+    v_local: torch.Tensor,
+    q_pos: torch.Tensor,
+    k_pos_local: torch.Tensor,
+    comm: Communicator,
+    *,
+    causal: bool = True,
+    scale: Optional[float] = None,
+    kv_map: KVMap = None,
+    kv_block: Optional[int] = None,
+) -> torch.Tensor:
+    """Replicated queries against a sequence-sharded cache (``sequence_parallel.py:250-280``).
+
+    Each rank attends over its shard (split-KV decode kernel); one all-gather
+    of ``[B, Sq, H, D+1]`` partials and an exact n-way merge follow.
+    """
+    o, l = attention_with_lse(q, k_local, v_local, q_pos, k_pos_local, causal=causal, scale=scale, kv_map=kv_map,
+                              kv_block=kv_block)
+    if comm.size == 1:
+        return o.to(q.dtype)
+    D = o.shape[-1]
+    packed = torch.cat([o, l.transpose(1, 2).unsqueeze(-1)], dim=-1)
+    parts = comm.all_gather_list(packed, dim=0)
+    outs: List[torch.Tensor] = [p[..., :D] for p in parts]
+    lses: List[torch.Tensor] = [p[..., D].transpose(1, 2) for p in parts]
+    out, _ = _merge(outs, lses, out_dtype=q.dtype)
+    return out
+
+
+__all__ = [
+    "distributed_kv_attention",
+    "gather_heads",
+    "gather_sequence",
+    "ring_attention",
+    "shard_sequence",
+    "ulysses_attention",
+    "ulysses_gather",
+    "ulysses_scatter",
+]

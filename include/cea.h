@@ -1,0 +1,171 @@
+/*
+ * cea.h — C ABI of the B200 sequence-parallel attention library (libcea.so).
+ *
+ * The library implements the compute of collab_infer's sequence-parallel
+ * attention path on sm_100a.  Every entry point takes plain pointers, sizes
+ * and strides (in elements), enqueues work on the given CUDA stream, never
+ * synchronises the host and never allocates: buffers, including workspaces,
+ * belong to the caller.  Functions return CEA_OK (0) or a positive error
+ * code; cea_last_error() gives the thread's last message.
+ *
+ * Tensor conventions (as in collab_infer):
+ *   q [B, Sq, Hq, D], k/v [B, Sk, Hkv, D], out [B, Sq, Hq, D]: token-major,
+ *     any strides for (b, s, h), the D axis contiguous;
+ *   lse [B, Hq, Sq] natural-log log-sum-exp, any strides;
+ *   positions [B, S] int64, -1 = padding; key j is visible to query i iff
+ *     k_pos[j] >= 0 && (!causal || k_pos[j] <= q_pos[i]);
+ *   rows with no visible key give out = 0 and lse = -inf.
+ */
+#ifndef CEA_H_
+#define CEA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CEA_ABI_VERSION 1
+
+enum cea_status {
+  CEA_OK = 0,
+  CEA_ERR_INVALID = 1,     /* bad argument (shapes, strides, null pointers) */
+  CEA_ERR_UNSUPPORTED = 2, /* dtype / shape combination without a kernel */
+  CEA_ERR_CUDA = 3,        /* CUDA runtime or driver error */
+  CEA_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+  CEA_ERR_DEVICE = 5       /* a kernel reported a device-side error (see cea_device_status) */
+};
+
+/* device-side error codes stored by kernels (bounded waits that expired) */
+enum cea_device_error {
+  CEA_DEV_OK = 0,
+  CEA_DEV_TIMEOUT_PRODUCER = 0x101,
+  CEA_DEV_TIMEOUT_MMA = 0x102,
+  CEA_DEV_TIMEOUT_SOFTMAX = 0x103,
+  CEA_DEV_TIMEOUT_DECODE = 0x104
+};
+
+typedef enum cea_dtype { CEA_F32 = 0, CEA_F16 = 1, CEA_BF16 = 2, CEA_F64 = 3 } cea_dtype;
+
+/*
+ * Attention with log-sum-exp over position-masked keys.
+ *
+ * Replaces collab_infer parallel/attention.py:201-239 (attention_with_lse),
+ * :270-301 (attention, lse == NULL) and, with accumulate = 1, the pairwise
+ * merge of :242-250 fused into the epilogue (the ring-attention step of
+ * parallel/sequence_parallel.py:117-121).
+ *
+ * in_dtype: q/k/v dtype.  out_dtype: dtype of out (F32 or F64 for the
+ * accumulation precision of attention_with_lse, or the input dtype for
+ * attention).  lse has dtype F64 when in_dtype is F64, else F32.
+ * accumulate = 1 merges the result into the (out, lse) already stored
+ * (requires lse and an F32/F64 out).
+ * kv_map (optional, length Hq, int32): KV head of every query head; NULL means
+ * query head h uses KV head h / (Hq / Hkv).
+ */
+typedef struct cea_attn_params {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  void* lse;
+  const int64_t* q_pos;
+  const int64_t* k_pos;
+  const int32_t* kv_map;
+  int64_t q_stride[3];   /* b, s, h */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int64_t lse_stride[3]; /* b, h, s */
+  int64_t qpos_stride[2]; /* b, s */
+  int64_t kpos_stride[2];
+  int32_t B, Sq, Sk, Hq, Hkv, D;
+  double scale;
+  int32_t causal;
+  int32_t in_dtype;
+  int32_t out_dtype;
+  int32_t accumulate;
+  void* workspace;
+  size_t workspace_bytes;
+} cea_attn_params;
+
+/* Bytes of workspace cea_attn_fwd needs for these parameters (0 if none). */
+size_t cea_attn_workspace_size(const cea_attn_params* p);
+
+/* Kernel cea_attn_fwd would run: 0 none (empty), 1 tcgen05 prefill, 2 split-KV decode, 3 SIMT. */
+int cea_attn_kernel_kind(const cea_attn_params* p);
+
+int cea_attn_fwd(const cea_attn_params* p, void* stream);
+
+/*
+ * Split-KV decode (few query rows per KV head against a long KV cache).
+ * Replaces the local attention of collab_infer parallel/sequence_parallel.py:270-272
+ * (distributed_kv_attention).  Same parameters as cea_attn_fwd; requires
+ * Sq * (Hq / Hkv) <= 16, uniform groups (kv_map NULL), bf16/f16, D in {64, 128}.
+ * The workspace holds the per-split partial results.
+ */
+int cea_decode_splitkv(const cea_attn_params* p, void* stream);
+
+/*
+ * Exact merge of n partial attention results over disjoint key sets.
+ * Replaces collab_infer parallel/attention.py:242-264 (merge_attention,
+ * merge_attention_list).  Partial i is (outs[i], lses[i]); all partials share
+ * the strides below.  out may alias outs[0] / lse may alias lses[0].
+ */
+#define CEA_MAX_MERGE 32
+typedef struct cea_merge_params {
+  int32_t n;
+  const void* outs[CEA_MAX_MERGE];
+  const void* lses[CEA_MAX_MERGE];
+  void* out;
+  void* lse; /* may be NULL */
+  int64_t part_o_stride[3];   /* b, s, h */
+  int64_t part_lse_stride[3]; /* b, h, s */
+  int64_t o_stride[3];
+  int64_t lse_stride[3];
+  int32_t B, Sq, H, D;
+  int32_t part_dtype; /* F32 or F64 (partials and lse) */
+  int32_t out_dtype;  /* F32, F64, BF16 or F16 */
+} cea_merge_params;
+
+int cea_merge(const cea_merge_params* p, void* stream);
+
+/*
+ * Segment copy for the Ulysses all-to-all (collab_infer
+ * parallel/sequence_parallel.py:163-177 and :191-194): segment i copies the
+ * [nb, ns, nh, D] block at src (strides src_stride, elements) to dst
+ * (strides dst_stride).  Used to pack per-peer head slices of q/k/v into one
+ * send buffer, to lay received blocks out as the full sequence and to put the
+ * returned head blocks back into [B, s, H, D].
+ */
+#define CEA_MAX_SEGMENTS 64
+typedef struct cea_segment {
+  const void* src;
+  void* dst;
+  int64_t src_stride[3]; /* b, s, h */
+  int64_t dst_stride[3];
+  int32_t nb, ns, nh;
+} cea_segment;
+
+typedef struct cea_copy_params {
+  int32_t n;
+  int32_t D;
+  int32_t elem_bytes; /* 2, 4 or 8 */
+  cea_segment seg[CEA_MAX_SEGMENTS];
+} cea_copy_params;
+
+int cea_ulysses_pack(const cea_copy_params* p, void* stream);
+int cea_ulysses_unpack(const cea_copy_params* p, void* stream);
+
+/* Reads (and with clear != 0 resets) the device error word of the current device. Synchronises `stream`. */
+int cea_device_status(int* status_out, int clear, void* stream);
+
+const char* cea_last_error(void);
+int cea_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CEA_H_ */

@@ -1,0 +1,35 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def load_golden(name: str) -> dict:
+    """``{case: {key: array}}`` from one of the reference-generated fixture files."""
+    data = np.load(os.path.join(GOLDEN, name), allow_pickle=False)
+    cases: dict = {}
+    for key in data.files:
+        case, _, rest = key.partition("/")
+        cases.setdefault(case, {})[rest] = data[key]
+    return cases
+
+
+@pytest.fixture(scope="session")
+def golden_single():
+    return load_golden("attention_single.npz")
+
+
+@pytest.fixture(scope="session")
+def golden_sp():
+    return load_golden("sequence_parallel.npz")
