@@ -12,12 +12,15 @@ positions ``[B, S]`` int64 with ``-1`` for padding, ``lse [B, Hq, Sq]``.
 from __future__ import annotations
 
 import math
+import os
 from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
 
-# queries per block: bounds the [B, Hkv, G*chunk, Sk] score buffer
-_ROWS_PER_CHUNK = 1 << 22
+# score elements per work item (bounds the [chunk, Sk] buffers)
+_ROWS_PER_CHUNK = 1 << 19
+# below this many score elements the oracle runs single-threaded
+_PARALLEL_WORK = 1 << 26
 
 
 def visibility(q_pos: np.ndarray, k_pos: np.ndarray, causal: bool = True) -> np.ndarray:
@@ -82,26 +85,38 @@ def attention_with_lse(
     heads = kv_index(Hq, Hkv, kv_map)
     kh = np.ascontiguousarray(k.astype(acc).transpose(0, 2, 1, 3))  # [B, Hkv, Sk, D]
     vh = np.ascontiguousarray(v.astype(acc).transpose(0, 2, 1, 3))
-    chunk = max(1, _ROWS_PER_CHUNK // max(1, Sk * Hq))
-    for s0 in range(0, Sq, chunk):
+    chunk = max(1, min(Sq, _ROWS_PER_CHUNK // max(1, Sk)))
+
+    def one(item):
+        b, h, s0 = item
         s1 = min(Sq, s0 + chunk)
-        vis = visibility(q_pos[:, s0:s1], k_pos, causal)  # [B, sq, Sk]
-        qc = q[:, s0:s1].astype(acc)
-        for h in range(Hq):
-            kvh = heads[h]
-            sc = np.matmul(qc[:, :, h, :], kh[:, kvh].transpose(0, 2, 1)) * acc(scale)  # [B, sq, Sk]
-            sc = np.where(vis, sc, -np.inf)
-            m = sc.max(axis=-1, keepdims=True)
-            m_safe = np.where(np.isfinite(m), m, 0.0)
-            p = np.exp(sc - m_safe)
-            l = p.sum(axis=-1, keepdims=True)
-            with np.errstate(divide="ignore"):
-                row_lse = (np.log(l) + m_safe)[..., 0]
-            row_lse = np.where(l[..., 0] > 0, row_lse, -np.inf)
-            o = np.matmul(p, vh[:, kvh])
-            o = np.where(l > 0, o / np.where(l > 0, l, 1.0), 0.0)
-            out[:, s0:s1, h] = o
-            lse[:, h, s0:s1] = row_lse
+        kvh = heads[h]
+        vis = visibility(q_pos[b : b + 1, s0:s1], k_pos[b : b + 1], causal)[0]  # [sq, Sk]
+        sc = np.matmul(q[b, s0:s1, h, :].astype(acc), kh[b, kvh].T) * acc(scale)
+        sc = np.where(vis, sc, -np.inf)
+        m = sc.max(axis=-1, keepdims=True)
+        m_safe = np.where(np.isfinite(m), m, 0.0)
+        p = np.exp(sc - m_safe)
+        l = p.sum(axis=-1, keepdims=True)
+        with np.errstate(divide="ignore"):
+            row_lse = (np.log(l) + m_safe)[..., 0]
+        lse[b, h, s0:s1] = np.where(l[..., 0] > 0, row_lse, -np.inf)
+        o = np.matmul(p, vh[b, kvh])
+        out[b, s0:s1, h] = np.where(l > 0, o / np.where(l > 0, l, 1.0), 0.0)
+
+    items = [(b, h, s0) for b in range(B) for h in range(Hq) for s0 in range(0, Sq, chunk)]
+    work = float(B) * Hq * Sq * Sk
+    if work < _PARALLEL_WORK or len(items) < 2:
+        for it in items:
+            one(it)
+    else:
+        # large problems (the timed CPU baseline): one work item per thread, BLAS single-threaded
+        from concurrent.futures import ThreadPoolExecutor
+
+        from threadpoolctl import threadpool_limits
+
+        with threadpool_limits(1), ThreadPoolExecutor(max_workers=os.cpu_count() or 1) as pool:
+            list(pool.map(one, items))
     return out, lse
 
 

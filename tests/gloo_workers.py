@@ -1,0 +1,168 @@
+"""Rank functions for the multi-process (gloo, CPU) tests.
+
+The sequence-parallel orchestration (who sends what to whom, uneven sizes,
+merge order, Ulysses packing) is host logic; on CPU ranks its compute calls
+are replaced by the oracle here, in the test only, so that the orchestration
+can be checked against the reference's golden vectors without a GPU.  The
+product itself never falls back to this: on a GPU it runs the CUDA kernels.
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import torch
+
+import oracle
+
+
+def install_oracle_compute():
+    import collaborative_edge_system_b200.sequence_parallel as sp
+
+    def kv_list(kv_map):
+        if kv_map is None:
+            return None
+        return [int(x) for x in (kv_map.tolist() if isinstance(kv_map, torch.Tensor) else kv_map)]
+
+    def npy(t):
+        return t.detach().cpu().numpy()
+
+    def attend_into(q, k, v, q_pos, k_pos, out, lse, *, causal=True, scale=None, kv_map=None, accumulate=False):
+        o, l = oracle.attention_with_lse(npy(q), npy(k), npy(v), npy(q_pos), npy(k_pos), causal, scale, kv_list(kv_map))
+        if accumulate:
+            o, l = oracle.merge_attention(npy(out).astype(np.float64), npy(lse).astype(np.float64), o, l)
+        out.copy_(torch.from_numpy(o))
+        if lse is not None:
+            lse.copy_(torch.from_numpy(l))
+
+    def attention_with_lse(q, k, v, q_pos, k_pos, *, causal=True, scale=None, kv_map=None, kv_block=None):
+        o, l = oracle.attention_with_lse(npy(q), npy(k), npy(v), npy(q_pos), npy(k_pos), causal, scale, kv_list(kv_map))
+        acc = torch.float64 if q.dtype == torch.float64 else torch.float32
+        return torch.from_numpy(o).to(acc), torch.from_numpy(l).to(acc)
+
+    def attention(q, k, v, q_pos, k_pos, *, causal=True, scale=None, kv_map=None, kv_block=None):
+        return attention_with_lse(q, k, v, q_pos, k_pos, causal=causal, scale=scale, kv_map=kv_map)[0].to(q.dtype)
+
+    def merge(outs, lses, out_dtype=None):
+        o, l = oracle.merge_attention_list([npy(x) for x in outs], [npy(x) for x in lses])
+        o = torch.from_numpy(np.asarray(o))
+        return o.to(out_dtype or outs[0].dtype), torch.from_numpy(np.asarray(l))
+
+    def copy_segments(pairs):
+        for src, dst in pairs:
+            dst.copy_(src)
+
+    sp.attend_into = attend_into
+    sp.attention_with_lse = attention_with_lse
+    sp.attention = attention
+    sp._merge = merge
+    sp._copy_segments = copy_segments
+
+
+def golden_inputs():
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "sequence_parallel.npz")
+    data = np.load(path)
+    return {k: torch.from_numpy(data[f"sp/{k}"]) for k in ("q", "k", "v", "pos")}
+
+
+def sp_worker(rank, world, kind, weights, causal):
+    """Ring, Ulysses and distributed-KV decode over gloo with the reference's SP test inputs."""
+    install_oracle_compute()
+    from collaborative_edge_system_b200 import ParallelContext, SequenceLayout, partition_heads
+    from collaborative_edge_system_b200.sequence_parallel import (
+        distributed_kv_attention,
+        ring_attention,
+        ulysses_attention,
+    )
+
+    ctx = ParallelContext(1, world, 1)
+    t = golden_inputs()
+    q, k, v, pos = t["q"], t["k"], t["v"], t["pos"]
+    S, HQ, HKV = q.shape[1], q.shape[2], k.shape[2]
+    layout = SequenceLayout(S, world, weights, kind)
+    ql, kl, vl, pl = (layout.shard(x, rank) for x in (q, k, v, pos))
+    ring, ring_lse = ring_attention(ql, kl, vl, pl, pl, ctx.sp, layout.sizes, causal=causal, return_lse=True)
+    shards = partition_heads(HQ, HKV, weights or world)
+    uly, (kh, vh, ph) = ulysses_attention(ql, kl, vl, pl, ctx.sp, layout.sizes, shards, causal=causal)
+    dkv = distributed_kv_attention(q[:, -2:], kl, vl, pos[:, -2:], pl, ctx.sp, causal=causal)
+    return {"ring": ring.numpy(), "ring_lse": ring_lse.numpy(), "ulysses": uly.numpy(), "k_heads": kh.numpy(),
+            "v_heads": vh.numpy(), "pos_full": ph.numpy(), "dkv": dkv.numpy(), "stats": ctx.stats.as_dict()}
+
+
+def ulysses_chunked_worker(rank, world):
+    install_oracle_compute()
+    from collaborative_edge_system_b200 import ParallelContext, SequenceLayout, partition_heads
+    from collaborative_edge_system_b200.sequence_parallel import gather_sequence, ulysses_attention
+
+    ctx = ParallelContext(1, world, 1)
+    t = golden_inputs()
+    q, k, v, pos = t["q"], t["k"], t["v"], t["pos"]
+    shards = partition_heads(q.shape[2], k.shape[2], world)
+    outs, past = [], None
+    for lo, hi in ((0, 7), (7, q.shape[1])):
+        layout = SequenceLayout(hi - lo, world)
+        sl = [layout.shard(x[:, lo:hi], rank) for x in (q, k, v, pos)]
+        o, (kh, vh, ph) = ulysses_attention(*sl, ctx.sp, layout.sizes, shards, past=past)
+        past = (kh, vh, ph) if past is None else tuple(torch.cat([a, b], 1) for a, b in zip(past, (kh, vh, ph)))
+        outs.append(gather_sequence(o, layout, ctx.sp))
+    return torch.cat(outs, dim=1).numpy()
+
+
+def collectives_worker(rank, world, fallback, small_bytes):
+    """The reference's uneven-collective checks (its tests/test_comm.py) on this Communicator."""
+    from collaborative_edge_system_b200 import ParallelContext
+
+    ctx = ParallelContext(1, 1, world, force_comm_fallback=fallback, small_message_bytes=small_bytes)
+    c = ctx.tp
+    sizes = [r + 1 for r in range(world)]
+    out = {}
+    out["all_reduce"] = c.all_reduce(torch.full((3,), float(rank + 1))).tolist()
+    out["all_reduce_max"] = c.all_reduce(torch.tensor([float(rank)]), op="max").item()
+    out["all_gather"] = c.all_gather(torch.full((2, rank + 1), float(rank)), dim=1, sizes=sizes).tolist()
+    full = torch.arange(2 * sum(sizes), dtype=torch.float64).view(2, -1) * (rank + 1)
+    out["reduce_scatter"] = c.reduce_scatter(full, dim=1, sizes=sizes).tolist()
+    ins = [torch.full((j + 1, rank + 1), float(rank * 10 + j)) for j in range(world)]
+    out["all_to_all"] = [t.tolist() for t in c.all_to_all(ins, [(rank + 1, j + 1) for j in range(world)])]
+    out["broadcast"] = c.broadcast(torch.arange(4.0) if rank == 1 else torch.zeros(4), src=1).tolist()
+    out["object"] = c.broadcast_object({"a": [1, 2]} if rank == 0 else None)
+    w = c.isend(torch.tensor([rank]), (rank + 1) % world)
+    out["ring"] = c.irecv((1,), torch.int64, (rank - 1) % world).wait().item()
+    w.wait()
+    # grouped ring step (what ring_attention uses): two tensors each way
+    got = c.ring_exchange([torch.full((2, 3), float(rank)), torch.tensor([rank, rank])], (rank + 1) % world,
+                          [((2, 3), torch.float32), ((2,), torch.int64)], (rank - 1) % world).wait()
+    out["ring_exchange"] = [got[0].tolist(), got[1].tolist()]
+    # flat uneven all-to-all
+    send = torch.cat([torch.full((j + 1,), float(rank * 10 + j)) for j in range(world)])
+    recv = torch.empty(world * (rank + 1))
+    c.all_to_all_single(recv, send, [rank + 1] * world, [j + 1 for j in range(world)]).wait()
+    out["all_to_all_single"] = recv.tolist()
+    out["calls"] = ctx.stats.total_calls
+    return out
+
+
+def compressed_worker(rank, world, comm_dtype):
+    from collaborative_edge_system_b200 import ParallelContext
+
+    ctx = ParallelContext(1, 1, world, comm_dtype=comm_dtype, small_message_bytes=0)
+    c = ctx.tp
+    x = torch.randn(64, 32, generator=torch.Generator().manual_seed(rank))
+    xs = [torch.randn(64, 32, generator=torch.Generator().manual_seed(r)) for r in range(world)]
+    total = sum(xs)
+    out = {
+        "exact": (c.all_reduce(x.clone()) - total).abs().max().item(),
+        "all_reduce": (c.all_reduce(x.clone(), compress=True) - total).abs().max().item(),
+        "all_gather": (c.all_gather(x, dim=0, compress=True) - torch.cat(xs)).abs().max().item(),
+        "reduce_scatter": (c.reduce_scatter(x.clone(), dim=0, compress=True) - total.chunk(world)[rank]).abs().max().item(),
+        "dtype": str(c.all_reduce(x.clone(), compress=True).dtype),
+    }
+    a2a = c.all_to_all(list(x.chunk(world)), [(64 // world, 32)] * world, compress=True)
+    out["all_to_all"] = max((a - xs[j].chunk(world)[rank]).abs().max().item() for j, a in enumerate(a2a))
+    return out
+
+
+def meta(case):
+    return json.loads(str(case["meta"]))

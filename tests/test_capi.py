@@ -1,0 +1,101 @@
+"""The C-ABI library loads on a machine without a GPU, exports every symbol of
+include/cea.h, and its structs have the layout the Python binding assumes."""
+
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from collaborative_edge_system_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "cea.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(cea_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_header_declares_the_binding_surface():
+    assert set(_declared()) == set(_lib.EXPORTS)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert lib.cea_abi_version() == 1
+
+
+def test_invalid_arguments_are_rejected_without_a_gpu():
+    lib = _lib.load()
+    p = _lib.AttnParams()
+    p.B, p.Sq, p.Sk, p.Hq, p.Hkv, p.D = 1, 4, 4, 3, 2, 64  # 3 query heads cannot share 2 KV heads
+    assert lib.cea_attn_fwd(ctypes.byref(p), None) == _lib.CEA_ERR_INVALID
+    assert b"cannot share" in lib.cea_last_error()
+    assert lib.cea_attn_workspace_size(ctypes.byref(p)) == 0
+    m = _lib.MergeParams()
+    m.n = 0
+    assert lib.cea_merge(ctypes.byref(m), None) == _lib.CEA_ERR_INVALID
+    c = _lib.CopyParams()
+    c.n, c.D, c.elem_bytes = 1, 8, 3
+    assert lib.cea_ulysses_pack(ctypes.byref(c), None) == _lib.CEA_ERR_INVALID
+
+
+def test_product_path_refuses_cpu_tensors():
+    import torch
+
+    import collaborative_edge_system_b200 as cea
+
+    q = torch.zeros(1, 4, 2, 64)
+    pos = torch.arange(4).view(1, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        cea.attention_with_lse(q, q, q, pos, pos)
+
+
+_LAYOUT_C = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "cea.h"
+#define P(s, f) printf(#s "." #f " %zu\n", offsetof(s, f))
+int main(void) {
+  printf("cea_attn_params %zu\n", sizeof(cea_attn_params));
+  P(cea_attn_params, q_stride); P(cea_attn_params, kpos_stride); P(cea_attn_params, B);
+  P(cea_attn_params, scale); P(cea_attn_params, accumulate); P(cea_attn_params, workspace_bytes);
+  printf("cea_merge_params %zu\n", sizeof(cea_merge_params));
+  P(cea_merge_params, out); P(cea_merge_params, lse_stride); P(cea_merge_params, out_dtype);
+  printf("cea_segment %zu\n", sizeof(cea_segment));
+  P(cea_segment, nh);
+  printf("cea_copy_params %zu\n", sizeof(cea_copy_params));
+  P(cea_copy_params, seg);
+  return 0;
+}
+"""
+
+
+def test_struct_layout_matches_ctypes():
+    with tempfile.TemporaryDirectory() as d:
+        src, exe = os.path.join(d, "layout.c"), os.path.join(d, "layout")
+        open(src, "w").write(_LAYOUT_C)
+        try:
+            subprocess.run(["gcc", "-I", os.path.dirname(HEADER), "-o", exe, src], check=True, capture_output=True)
+        except (OSError, subprocess.CalledProcessError) as exc:
+            pytest.skip(f"no C compiler: {exc}")
+        out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout
+    c = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
+    c = {k: int(v) for k, v in c.items()}
+    assert c["cea_attn_params"] == ctypes.sizeof(_lib.AttnParams)
+    assert c["cea_merge_params"] == ctypes.sizeof(_lib.MergeParams)
+    assert c["cea_segment"] == ctypes.sizeof(_lib.Segment)
+    assert c["cea_copy_params"] == ctypes.sizeof(_lib.CopyParams)
+    for key, val in c.items():
+        if "." in key:
+            struct, field = key.split(".")
+            cls = {"cea_attn_params": _lib.AttnParams, "cea_merge_params": _lib.MergeParams,
+                   "cea_segment": _lib.Segment, "cea_copy_params": _lib.CopyParams}[struct]
+            assert getattr(cls, field).offset == val, key

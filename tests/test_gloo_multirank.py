@@ -1,0 +1,78 @@
+"""Multi-rank host logic on gloo CPU ranks: the Communicator's uneven collectives and the
+ring / Ulysses / distributed-KV orchestration against the reference's golden vectors."""
+
+import numpy as np
+import pytest
+import torch
+
+import gloo_workers as W
+from collaborative_edge_system_b200 import SequenceLayout, launch_local
+
+CASES = [(2, "contiguous", None, True), (2, "zigzag", None, True), (3, "zigzag", [3, 2, 1], True),
+         (3, "contiguous", [1, 2, 3], False)]
+
+
+def _run(fn, world, *args):
+    return launch_local(fn, world, args=args, return_results=True, threads_per_rank=1, timeout_s=120)
+
+
+@pytest.mark.parametrize("ci", range(4))
+def test_sequence_parallel_orchestration_matches_reference(golden_sp, ci):
+    world, kind, weights, causal = CASES[ci]
+    gold = golden_sp[f"sp{ci}"]
+    base = golden_sp["sp"]
+    pos = torch.from_numpy(base["pos"])
+    lay = SequenceLayout(pos.shape[1], world, weights, kind)
+    full_lse = gold["full_lse"]
+    for r, res in enumerate(_run(W.sp_worker, world, kind, weights, causal)):
+        valid = lay.shard(pos, r).numpy() >= 0
+        for key in ("ring", "ulysses"):
+            err = np.abs(res[key] - gold[f"r{r}/{key}"])[valid].max()
+            assert err < 1e-12, (key, r, err)
+        for key in ("k_heads", "v_heads", "pos_full", "dkv"):
+            assert np.abs(res[key] - gold[f"r{r}/{key}"]).max() < 1e-12, (key, r)
+        idx = lay.indices(r).numpy()
+        want = full_lse[:, :, idx]
+        got = res["ring_lse"]
+        both = np.isinf(want) & np.isinf(got)
+        with np.errstate(invalid="ignore"):
+            diff = np.where(both, 0, np.abs(got - want))
+        assert diff[valid[:, None, :].repeat(want.shape[1], 1)].max() < 1e-12
+        assert res["stats"]["sp.send"]["calls"] >= world - 1
+
+
+def test_ulysses_prefill_on_top_of_cache(golden_sp):
+    gold = golden_sp["ulysses_chunked"]
+    for r, full in enumerate(_run(W.ulysses_chunked_worker, 3)):
+        assert np.abs(full - gold[f"r{r}/full"]).max() < 1e-12
+
+
+@pytest.mark.parametrize("fallback,small_bytes", [(False, 0), (True, 0), (False, 1 << 16)],
+                         ids=["native", "fallback", "direct-small-messages"])
+def test_collectives_with_uneven_sizes(fallback, small_bytes):
+    world = 3
+    total = torch.arange(2 * 6, dtype=torch.float64).view(2, -1) * 6
+    for rank, out in enumerate(_run(W.collectives_worker, world, fallback, small_bytes)):
+        assert out["all_reduce"] == [6.0] * 3
+        assert out["all_reduce_max"] == 2.0
+        assert out["all_gather"] == [[0.0, 1.0, 1.0, 2.0, 2.0, 2.0]] * 2
+        start = sum(range(1, rank + 1))
+        assert out["reduce_scatter"] == total[:, start : start + rank + 1].tolist()
+        for j, t in enumerate(out["all_to_all"]):
+            assert torch.equal(torch.tensor(t), torch.full((rank + 1, j + 1), float(j * 10 + rank)))
+        assert out["broadcast"] == [0.0, 1.0, 2.0, 3.0]
+        assert out["object"] == {"a": [1, 2]}
+        prev = (rank - 1) % world
+        assert out["ring"] == prev
+        assert out["ring_exchange"] == [[[float(prev)] * 3] * 2, [prev, prev]]
+        assert out["all_to_all_single"] == sum(([float(j * 10 + rank)] * (rank + 1) for j in range(world)), [])
+        assert out["calls"] > 0
+
+
+@pytest.mark.parametrize("comm_dtype,tol", [("float16", 5e-3), ("bfloat16", 5e-2)])
+def test_compressed_collectives(comm_dtype, tol):
+    for out in _run(W.compressed_worker, 2, comm_dtype):
+        assert out["exact"] < 1e-6
+        assert out["dtype"] == "torch.float32"
+        for key in ("all_reduce", "all_gather", "reduce_scatter", "all_to_all"):
+            assert out[key] < tol, (key, out[key])

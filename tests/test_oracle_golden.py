@@ -21,7 +21,8 @@ def _close(a, b, tol):
     a, b = np.asarray(a), np.asarray(b)
     assert a.shape == b.shape
     both_inf = np.isinf(a) & np.isinf(b) & (np.sign(a) == np.sign(b))
-    diff = np.where(both_inf, 0.0, np.abs(a.astype(np.float64) - b.astype(np.float64)))
+    with np.errstate(invalid="ignore"):
+        diff = np.where(both_inf, 0.0, np.abs(a.astype(np.float64) - b.astype(np.float64)))
     assert not np.isnan(diff).any()
     assert diff.max(initial=0.0) <= tol, diff.max()
 
