@@ -353,6 +353,39 @@ def cpu_baseline(seconds_target: float = 15.0):
                       f"fp32 numpy oracle ({dt:.1f} s)"}
 
 
+# ----------------------------------------------------------------------------- profiling cases
+def ncu_case(which: str, warmup: int) -> None:
+    """A few launches of one kernel on a case sized for an ncu capture.
+
+    prefill: causal GQA attention, 16384 tokens (q 128 MiB + k/v 32 MiB each: inputs beyond L2),
+    1/16 of the benchmark's queries x 1/8 of its keys on average -> one launch of attn_fwd_tc_kernel
+    per call.  decode: the benchmark's decode shape with a 16384-token cache (512 MiB of K+V).
+    """
+    import collaborative_edge_system_b200 as cea
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    if which == "prefill":
+        S = 16384
+        q = (torch.randn(1, S, HQ, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+        k = torch.randn(1, S, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(1, S, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+        pos = torch.arange(S, device=dev).view(1, S)
+        for _ in range(warmup + 1):
+            cea.attention_with_lse(q, k, v, pos, pos, causal=True)
+    else:
+        T = 16384
+        q = torch.randn(DEC_B, 1, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+        kc = torch.randn(DEC_B, HKV, T + 64, D, generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn(DEC_B, HKV, T + 64, D, generator=g, device=dev).to(torch.bfloat16)
+        kpos = torch.arange(T, device=dev).repeat(DEC_B, 1)
+        qpos = torch.full((DEC_B, 1), T, device=dev)
+        for _ in range(warmup + 1):
+            cea.attention_with_lse(q, kc[:, :, :T].transpose(1, 2), vc[:, :, :T].transpose(1, 2), qpos, kpos)
+    torch.cuda.synchronize()
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -362,7 +395,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ncu-case", choices=["prefill", "decode"], default=None,
+                    help="run a small case of one kernel for an ncu capture (no timing, no JSON line)")
     args = ap.parse_args()
+    if args.ncu_case:
+        ncu_case(args.ncu_case, max(1, args.warmup))
+        return
 
     config = {"workload": "zigzag causal ring-attention prefill, LLaMA-3-8B attention shape",
               "batch": 1, "seq_len": S_TOTAL, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,

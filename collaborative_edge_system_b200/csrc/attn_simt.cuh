@@ -238,8 +238,10 @@ struct MergeArgs {
   int B, Sq, H, D;
 };
 
+constexpr int kMergeWarps = 8;  // merge_kernel is launched with 256 threads
+
 template <typename P, typename O>
-__global__ void merge_kernel(const MergeArgs a) {
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeArgs a) {
   const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (wid >= static_cast<int64_t>(a.B) * a.Sq * a.H) return;
@@ -264,15 +266,17 @@ __global__ void merge_kernel(const MergeArgs a) {
     lse = mx + simt::log_acc<P>(e);
   }
   const P safe = lse == P(-INFINITY) ? P(0) : lse;
-  const P wi = lane < a.n ? simt::exp_acc<P>(li - safe) : P(0);
+  // the weights go through shared memory: lanes past D leave the column loop early,
+  // so no shuffle may sit inside it
+  __shared__ P wsm[kMergeWarps][CEA_MAX_MERGE];
+  const int wslot = threadIdx.x >> 5;
+  if (lane < a.n) wsm[wslot][lane] = simt::exp_acc<P>(li - safe);
+  __syncwarp();
   const int64_t ooff = b * a.po_sb + static_cast<int64_t>(s) * a.po_ss + h * a.po_sh;
   O* dst = reinterpret_cast<O*>(a.out) + b * a.o_sb + static_cast<int64_t>(s) * a.o_ss + h * a.o_sh;
   for (int d = lane; d < a.D; d += 32) {
     P acc = P(0);
-    for (int i = 0; i < a.n; ++i) {
-      const P w = __shfl_sync(0xffffffffu, wi, i);
-      acc += reinterpret_cast<const P*>(a.outs[i])[ooff + d] * w;
-    }
+    for (int i = 0; i < a.n; ++i) acc += reinterpret_cast<const P*>(a.outs[i])[ooff + d] * wsm[wslot][i];
     simt::store_as<O, P>(dst + d, acc);
   }
   // the partial lse values are all read (li) before any lane writes the merged one

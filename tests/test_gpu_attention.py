@@ -14,7 +14,7 @@ import torch
 
 import oracle
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.timeout(180)]
 
 cea = pytest.importorskip("collaborative_edge_system_b200")
 from collaborative_edge_system_b200 import _lib  # noqa: E402
