@@ -20,6 +20,7 @@ same workload; rank 0 alone runs it.
 from __future__ import annotations
 
 import argparse
+import importlib
 import json
 import math
 import os
@@ -163,7 +164,7 @@ def bench_prefill(cea, rank, world, dev, steps, warmup):
     my_flops = 4.0 * HQ * D * visible_pairs(idx)
 
     # instrument the attention launches (events on the launching stream) without changing the step
-    from collaborative_edge_system_b200 import attention as attn_mod
+    attn_mod = importlib.import_module("collaborative_edge_system_b200.attention")
 
     orig = attn_mod.attend_into
     ev = []
@@ -247,7 +248,7 @@ def bench_prefill_e2e(cea, rank, world, dev, steps, warmup, layout, tensors, com
 
 # ----------------------------------------------------------------------------- ours: decode
 def bench_decode(cea, rank, world, dev):
-    from collaborative_edge_system_b200 import attention as attn_mod
+    from collaborative_edge_system_b200 import _lib
 
     T_loc = [DEC_T // world + (1 if r < DEC_T % world else 0) for r in range(world)]
     start_pos = sum(T_loc[:rank])
@@ -262,7 +263,7 @@ def bench_decode(cea, rank, world, dev):
     owner = world - 1
     scale = 1.0 / math.sqrt(D)
     ev = []
-    orig = attn_mod._lib.attn_fwd
+    orig = _lib.attn_fwd
 
     def timed_fwd(p, device, entry="cea_attn_fwd"):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -293,14 +294,14 @@ def bench_decode(cea, rank, world, dev):
     for _ in range(DEC_WARM):
         step()
     barrier(world)
-    attn_mod._lib.attn_fwd = timed_fwd
+    _lib.attn_fwd = timed_fwd
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(DEC_STEPS):
         step()
     t1.record()
     barrier(world)
-    attn_mod._lib.attn_fwd = orig
+    _lib.attn_fwd = orig
     ms = max_over_ranks(t0.elapsed_time(t1), world, dev)
     kern_ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
     avg_len = state["length"] - DEC_STEPS / 2 if rank == owner else state["length"]

@@ -4,11 +4,13 @@
 // cea_device_status, which exists to do exactly that) or allocates memory.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
 #include "attn_simt.cuh"
 #include "attn_tc.cuh"
+#include "attn_tc2.cuh"
 #include "cea_common.cuh"
 #include "decode.cuh"
 
@@ -214,6 +216,19 @@ int launch_empty(const cea_attn_params* p, cudaStream_t s) {
   return cuda_check("fill_empty_kernel");
 }
 
+// which prefill kernel generation runs (CEA_PREFILL_KERNEL=1 selects the single-tile kernel)
+int prefill_version() {
+  static int v = [] {
+    const char* e = getenv("CEA_PREFILL_KERNEL");
+    return (e != nullptr && e[0] == '1') ? 1 : 2;
+  }();
+  return v;
+}
+
+// with an explicit kv_map, heads 2i and 2i+1 must read the same KV head to share a CTA.
+// The map lives on the device, so only the uniform grouping is paired here.
+bool kv_pairs_ok(const cea_attn_params*) { return false; }
+
 int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   const size_t need = tc_stats_bytes(p);
   if (p->workspace == nullptr || p->workspace_bytes < need)
@@ -268,13 +283,35 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   tp.accumulate = p->accumulate;
   const int64_t grid = static_cast<int64_t>(nqt) * p->Hq * p->B;
   if (grid > 0x7fffffff) return fail(CEA_ERR_UNSUPPORTED, "grid too large");
+  const bool bf = p->in_dtype == CEA_BF16;
+  if (prefill_version() == 2) {
+    // two query tiles per CTA: a GQA head pair when heads pair up on one KV head, else adjacent q tiles
+    tc2::Params pp;
+    pp.base = tp;
+    const bool heads_pair = p->Hq % 2 == 0 && (p->kv_map == nullptr ? (p->Hq / p->Hkv) % 2 == 0 : kv_pairs_ok(p));
+    pp.pair_heads = heads_pair ? 1 : 0;
+    pp.nblk_q = heads_pair ? nqt : (nqt + 1) / 2;
+    const int64_t grid2 = static_cast<int64_t>(pp.nblk_q) * p->B * (heads_pair ? p->Hq / 2 : p->Hq);
+#define CEA_TC2(DD, BF)                                                                                        \
+  do {                                                                                                         \
+    auto k = tc2::attn_fwd_tc2_kernel<DD, BF>;                                                                 \
+    allow_smem(k, tc2::Layout<DD>::SMEM_ALLOC);                                                                \
+    k<<<static_cast<unsigned>(grid2), tc2::NUM_THREADS, tc2::Layout<DD>::SMEM_ALLOC, s>>>(mq, mk, mv, pp);     \
+  } while (0)
+    if (p->D == 128) {
+      if (bf) CEA_TC2(128, true); else CEA_TC2(128, false);
+    } else {
+      if (bf) CEA_TC2(64, true); else CEA_TC2(64, false);
+    }
+#undef CEA_TC2
+    return cuda_check("attn_fwd_tc2_kernel");
+  }
 #define CEA_TC(DD, BF)                                                                                       \
   do {                                                                                                       \
     auto k = tc::attn_fwd_tc_kernel<DD, BF>;                                                                 \
     allow_smem(k, tc::Layout<DD>::SMEM_ALLOC);                                                               \
     k<<<static_cast<unsigned>(grid), tc::NUM_THREADS, tc::Layout<DD>::SMEM_ALLOC, s>>>(mq, mk, mv, tp);      \
   } while (0)
-  const bool bf = p->in_dtype == CEA_BF16;
   if (p->D == 128) {
     if (bf) CEA_TC(128, true); else CEA_TC(128, false);
   } else {
