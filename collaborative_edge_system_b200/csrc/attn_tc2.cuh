@@ -95,7 +95,7 @@ __device__ __forceinline__ float exp2_poly3(float x) {
 }
 
 template <int D, bool kBF16>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const Params pp) {
   using L = Layout<D>;

@@ -52,8 +52,13 @@ def _entry(rank: int, fn: Callable[..., Any], world: int, port: int, backend: st
     if env:
         os.environ.update(env)
     torch.set_num_threads(max(1, threads))
+    kw = {}
+    if backend == "nccl":  # one GPU per rank, bound before the communicator is created
+        dev = torch.device("cuda", rank % torch.cuda.device_count())
+        torch.cuda.set_device(dev)
+        kw["device_id"] = dev
     dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            timeout=timedelta(seconds=timeout_s))
+                            timeout=timedelta(seconds=timeout_s), **kw)
     try:
         res = fn(rank, world, *args)
         if queue is not None:

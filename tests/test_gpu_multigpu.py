@@ -1,0 +1,41 @@
+"""Multi-GPU parity over NCCL (one process per GPU): ring (zigzag / uneven, GQA, padding),
+Ulysses (uneven heads and tokens) and distributed-KV decode against the oracle."""
+
+import pytest
+import torch
+
+import gpu_workers as W
+from collaborative_edge_system_b200 import launch_local
+
+pytestmark = [pytest.mark.gpu, pytest.mark.timeout(300)]
+
+
+def _gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _run(fn, world, *args):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    return launch_local(fn, world, args=args, backend="nccl", return_results=True, timeout_s=120,
+                        env={"NCCL_NVLS_ENABLE": "0"})
+
+
+@pytest.mark.parametrize("kind,weights,S,pad", [("zigzag", None, 1024, 0), ("contiguous", [3, 1], 1000, 45),
+                                                ("zigzag", [1, 2], 777, 0)])
+def test_ring_attention_nccl(kind, weights, S, pad):
+    for eo, el, stats in _run(W.ring_worker, 2, kind, weights, S, 8, 2, 128, pad):
+        assert eo < 2e-2 and el < 1e-3, (eo, el)
+        assert stats["sp.send"]["calls"] == 1
+
+
+def test_ulysses_attention_nccl():
+    for eo, ek in _run(W.ulysses_worker, 2, [3, 1], 512, 8, 8, 128):
+        assert eo < 2e-2
+        assert ek == 0.0
+
+
+def test_distributed_kv_decode_nccl():
+    for eo, dtype in _run(W.decode_worker, 2, 3000, 4, 8, 2, 128):
+        assert eo < 2e-2
+        assert dtype == "torch.bfloat16"
