@@ -5,6 +5,7 @@
 // query tiles of one head.  Every K/V tile is loaded once for both halves.
 //   warps 0-3 / 4-7   softmax of half 0 / half 1 (one thread per row = TMEM lane)
 //   warp 8            TMA producer (Q0, Q1, then a K ring and a V ring)
+//   warps 10-11       idle (they complete the third warpgroup for setmaxnreg)
 //   warp 9            MMA issuer, one thread:
 //                       S_h = Q_h K^T           (SS form, fp32 into TMEM)
 //                       O_h += P_h V            (TS form: P_h read from TMEM, V from smem)
@@ -17,6 +18,11 @@
 // S_h(t) complete, PV_h(t-1) has completed too: O_h may be rescaled and the
 // P_h columns rewritten without further waits.  The halves alternate, so one
 // half's softmax overlaps the other half's MMAs.
+//
+// Registers: the softmax warpgroups raise their budget to 232 with setmaxnreg
+// while the producer/MMA warpgroup drops to 40 (232 + 232 + 40 per SMSP stays
+// within the 168 x 3 the launch reserves), so a softmax thread holds its whole
+// S row in registers and reads TMEM with a single wait.
 //
 // Exponentials: ex2.approx on the MUFU pipe, except 3 of every 8 elements of
 // fully visible tiles, which use exp2_poly3 on the FMA pipe (round-to-nearest
@@ -31,7 +37,7 @@ namespace tc2 {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int NUM_THREADS = 320;
+constexpr int NUM_THREADS = 384;  // three warpgroups: softmax 0, softmax 1, producer + MMA (+2 idle)
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
@@ -178,6 +184,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
+  }
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------------- TMA producer
@@ -253,11 +264,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t kbase = sbase + L::OFF_K + ks * L::TILE;
         for (int h = 0; h < 2; ++h) {
-          if ((h == 0 ? c0 : c1) == kSkip) continue;
+          // a pending PV is issued no later than the next union tile, even when this half skips
+          // it: the V stage it holds is what the producer needs next
           if (prev_u[h] >= 0 && !issue_pv(h)) {
             ok = false;
             break;
           }
+          if ((h == 0 ? c0 : c1) == kSkip) continue;
           const uint32_t tS = tmem + 256 * h;
           const uint32_t qbase = sbase + L::OFF_Q + h * L::TILE;
 #pragma unroll
@@ -278,7 +291,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int h = 0; ok && h < 2; ++h)
         if (prev_u[h] >= 0) ok = issue_pv(h);
     }
-  } else {
+  } else if (warp < 8) {
     // ---------------------------------------------------------------- softmax + epilogue (per half)
     const int h = warp >> 2;
     const int row = threadIdx.x & 127;
@@ -301,17 +314,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        // pass 1: row max of the raw scores, 32 columns at a time (the scale is positive, so it
-        // commutes with max); masked tiles also record each key's visibility as a bit
-        uint32_t vis_bits[BN / 32];
-        float rmax = -INFINITY;
+        // the whole S row in registers, one TMEM wait
+        uint32_t r[BN];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tS + c * 32, r);
-          uint32_t bits = 0xffffffffu;
-          if (cls == kMasked) {
-            bits = 0u;
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+        uint32_t vis_bits[BN / 32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) vis_bits[c] = 0xffffffffu;
+        if (cls == kMasked) {  // overlaps the TMEM load
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t bits = 0u;
             const int kbase = kt * BN + c * 32;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
@@ -319,13 +332,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const long long kp = key < p.Sk ? kpos_b[static_cast<int64_t>(key) * p.kpos_ss] : -1ll;
               bits |= (kp >= 0 && (!causal || kp <= qpos)) ? (1u << e) : 0u;
             }
+            vis_bits[c] = bits;
           }
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            rmax = fmaxf(rmax, ((bits >> e) & 1u) ? __uint_as_float(r[e]) : -INFINITY);
-          vis_bits[c] = bits;
         }
+        tmem_wait_ld();
+        // the scale is positive, so it commutes with max
+        float rmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < BN; ++j)
+          rmax = fmaxf(rmax, ((vis_bits[j >> 5] >> (j & 31)) & 1u) ? __uint_as_float(r[j]) : -INFINITY);
         const float tmax = rmax * p.scale_log2;
         const float m_new = fmaxf(m, tmax);
         const bool rescale = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
@@ -350,21 +365,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(tO + c * 32, o);
           }
         }
-        // pass 2: P = 2^(s*scale - m) as 16-bit pairs; chunk c lands in columns [16c, 16c+16),
-        // which pass 2 has already read (chunk c/2), so S is never overwritten before use
+        // P = 2^(s*scale - m) as 16-bit pairs over the first 64 S columns (already in registers)
         float rowsum = 0.f;
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tS + c * 32, r);
-          tmem_wait_ld();
           uint32_t pk[16];
           const uint32_t bits = vis_bits[c];
           if (cls == kFull) {
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const float x0 = fmaf(__uint_as_float(r[2 * e]), p.scale_log2, -m_use);
-              const float x1 = fmaf(__uint_as_float(r[2 * e + 1]), p.scale_log2, -m_use);
+              const float x0 = fmaf(__uint_as_float(r[c * 32 + 2 * e]), p.scale_log2, -m_use);
+              const float x1 = fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), p.scale_log2, -m_use);
               // elements 5, 6, 7 of every 8 on the FMA pipe, the rest on MUFU
               const float p0 = ((2 * e) & 7) >= 5 ? exp2_poly3(x0) : fast_exp2(x0);
               const float p1 = ((2 * e + 1) & 7) >= 5 ? exp2_poly3(x1) : fast_exp2(x1);
@@ -374,9 +385,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           } else {
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const float x0 = ((bits >> (2 * e)) & 1u) ? fmaf(__uint_as_float(r[2 * e]), p.scale_log2, -m_use) : -INFINITY;
-              const float x1 =
-                  ((bits >> (2 * e + 1)) & 1u) ? fmaf(__uint_as_float(r[2 * e + 1]), p.scale_log2, -m_use) : -INFINITY;
+              const float x0 = ((bits >> (2 * e)) & 1u) ? fmaf(__uint_as_float(r[c * 32 + 2 * e]), p.scale_log2, -m_use)
+                                                        : -INFINITY;
+              const float x1 = ((bits >> (2 * e + 1)) & 1u)
+                                   ? fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), p.scale_log2, -m_use)
+                                   : -INFINITY;
               const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
               rowsum += p0 + p1;
               pk[e] = pack2(p0, p1, kBF16);

@@ -216,11 +216,11 @@ int launch_empty(const cea_attn_params* p, cudaStream_t s) {
   return cuda_check("fill_empty_kernel");
 }
 
-// which prefill kernel generation runs (CEA_PREFILL_KERNEL=1 selects the single-tile kernel)
+// which prefill kernel generation runs (CEA_PREFILL_KERNEL=2 selects the two-tile kernel under evaluation)
 int prefill_version() {
   static int v = [] {
     const char* e = getenv("CEA_PREFILL_KERNEL");
-    return (e != nullptr && e[0] == '1') ? 1 : 2;
+    return (e != nullptr && e[0] == '2') ? 2 : 1;
   }();
   return v;
 }
