@@ -184,12 +184,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp < 8) {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
-  } else {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
-  }
-
+  if (warp >= 8) {
+  // ==================================================================== warpgroup 2
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
@@ -291,8 +288,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int h = 0; ok && h < 2; ++h)
         if (prev_u[h] >= 0) ok = issue_pv(h);
     }
-  } else if (warp < 8) {
-    // ---------------------------------------------------------------- softmax + epilogue (per half)
+  }
+  } else {
+    // ==================================================================== warpgroups 0, 1: softmax + epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
     const int h = warp >> 2;
     const int row = threadIdx.x & 127;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
