@@ -22,6 +22,7 @@ _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, tor
 CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE = range(6)
 MAX_MERGE = 32
 MAX_SEGMENTS = 64
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 KIND_NONE, KIND_TC, KIND_DECODE, KIND_SIMT = 0, 1, 2, 3
 
@@ -108,6 +109,7 @@ EXPORTS = (
     "cea_attn_workspace_size",
     "cea_attn_kernel_kind",
     "cea_decode_splitkv",
+    "cea_decode_splitkv_noalloc",
     "cea_merge",
     "cea_ulysses_pack",
     "cea_ulysses_unpack",
@@ -136,6 +138,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         for name, args, res in (
             ("cea_attn_fwd", [ctypes.POINTER(AttnParams), P], ctypes.c_int),
             ("cea_decode_splitkv", [ctypes.POINTER(AttnParams), P], ctypes.c_int),
+            ("cea_decode_splitkv_noalloc", [ctypes.POINTER(AttnParams), P], ctypes.c_int),
             ("cea_attn_workspace_size", [ctypes.POINTER(AttnParams)], ctypes.c_size_t),
             ("cea_attn_kernel_kind", [ctypes.POINTER(AttnParams)], ctypes.c_int),
             ("cea_merge", [ctypes.POINTER(MergeParams), P], ctypes.c_int),

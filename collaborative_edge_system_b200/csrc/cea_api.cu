@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "attn_simt.cuh"
@@ -155,15 +156,20 @@ struct DecodePlan {
   size_t part_bytes;
 };
 
-DecodePlan decode_plan(const cea_attn_params* p) {
+// max_bytes bounds the partials' size (the fixed scratch of cea_decode_splitkv_noalloc);
+// nsplit is 0 when not even one split fits
+DecodePlan decode_plan(const cea_attn_params* p, size_t max_bytes = SIZE_MAX) {
   const int nkt = (p->Sk + dec::BKEYS - 1) / dec::BKEYS;
   const int per_sm = p->D == 128 ? 2 : 3;  // resident CTAs per SM (shared-memory bound)
   const int slots = num_sms() * per_sm;
   const int64_t pairs = static_cast<int64_t>(p->B) * p->Hkv;
+  const size_t split_bytes = static_cast<size_t>(p->B) * p->Hq * p->Sq * (p->D + 1) * sizeof(float);
+  const size_t fit = split_bytes ? max_bytes / split_bytes : 0;
   // pick the split count minimising (waves x tiles per split), preferring fewer splits on ties
   int best = 1;
   double best_cost = 1e30;
-  const int max_split = std::max(1, std::min(256, nkt));
+  const int max_split = std::max(1, std::min(std::min(256, nkt), static_cast<int>(std::min<size_t>(fit, 256))));
+  if (fit == 0) return DecodePlan{0, 0, split_bytes};
   for (int ns = 1; ns <= max_split; ++ns) {
     const int tps = (nkt + ns - 1) / ns;
     const int used = (nkt + tps - 1) / tps;
@@ -321,11 +327,18 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   return cuda_check("attn_fwd_tc_kernel");
 }
 
+int launch_decode_plan(const cea_attn_params* p, cudaStream_t s, const DecodePlan& plan, void* workspace);
+
 int launch_decode(const cea_attn_params* p, cudaStream_t s) {
   const DecodePlan plan = decode_plan(p);
   if (p->workspace == nullptr || p->workspace_bytes < plan.part_bytes)
     return fail(CEA_ERR_WORKSPACE, "split-KV decode needs %zu workspace bytes, got %zu", plan.part_bytes,
                 p->workspace_bytes);
+  return launch_decode_plan(p, s, plan, p->workspace);
+}
+
+// the partials live in `workspace` (plan.part_bytes of it)
+int launch_decode_plan(const cea_attn_params* p, cudaStream_t s, const DecodePlan& plan, void* workspace) {
   CUtensorMap mk, mv;
   if (!make_map(&mk, p->in_dtype, p->k, p->D, p->Sk, p->Hkv, p->B, p->k_stride[1], p->k_stride[2], p->k_stride[0],
                 dec::BKEYS) ||
@@ -344,7 +357,7 @@ int launch_decode(const cea_attn_params* p, cudaStream_t s) {
   dp.k_pos = p->k_pos;
   dp.kpos_sb = p->kpos_stride[0];
   dp.kpos_ss = p->kpos_stride[1];
-  dp.part_o = reinterpret_cast<float*>(p->workspace);
+  dp.part_o = reinterpret_cast<float*>(workspace);
   dp.part_lse = dp.part_o + rows * plan.nsplit * p->D;
   dp.B = p->B;
   dp.Sq = p->Sq;
@@ -515,6 +528,72 @@ int cea_decode_splitkv(const cea_attn_params* p, void* stream) {
     return fail(CEA_ERR_UNSUPPORTED,
                 "split-KV decode needs bf16/f16, D in {64,128}, uniform GQA, Sq*group <= 16 and TMA-aligned K/V");
   return launch_decode(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Split-KV decode for callers that cannot allocate device memory.
+//
+// The per-split partials live in a file-scope device array instead of a
+// caller-provided workspace.  Host code must not use the array's name as a
+// device address: its address is obtained once per device, with that device
+// current, through cudaGetSymbolAddress, and passed to the kernels.  The array
+// is shared by every call on a device, so calls that overlap on the GPU (on
+// different streams) race on it.  Nothing in it has to start at zero: every
+// partial the combine step reads is written by the same call first.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CEA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+// device address of g_noalloc_scratch on the current device (looked up on the first call there)
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  const cudaError_t ge = cudaGetDevice(&dev);
+  if (ge != cudaSuccess) return fail(CEA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(ge));
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(CEA_ERR_UNSUPPORTED, "device %d is beyond the %d devices the decode scratch table covers", dev,
+                kNoallocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(CEA_ERR_CUDA, "cudaGetSymbolAddress of the decode scratch on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return CEA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cea_decode_splitkv_noalloc(const cea_attn_params* p, void* stream) {
+  if (int e = validate(p)) return e;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (p->B == 0 || p->Sq == 0 || p->Hq == 0) return CEA_OK;
+  if (p->Sk == 0) return p->accumulate ? CEA_OK : launch_empty(p, s);
+  if (!decode_ok(p))
+    return fail(CEA_ERR_UNSUPPORTED,
+                "split-KV decode needs bf16/f16, D in {64,128}, uniform GQA, Sq*group <= 16 and TMA-aligned K/V");
+  const DecodePlan plan = decode_plan(p, CEA_NOALLOC_SCRATCH_BYTES);
+  if (plan.nsplit == 0)
+    return fail(CEA_ERR_WORKSPACE,
+                "allocation-free decode: one split of partials for B*Hq*Sq = %lld rows needs %zu bytes, more than the "
+                "fixed %u-byte scratch",
+                static_cast<long long>(p->B) * p->Hq * p->Sq, plan.part_bytes,
+                static_cast<unsigned>(CEA_NOALLOC_SCRATCH_BYTES));
+  void* scratch = nullptr;
+  if (int e = noalloc_scratch(&scratch)) return e;
+  return launch_decode_plan(p, s, plan, scratch);
 }
 
 int cea_merge(const cea_merge_params* p, void* stream) {

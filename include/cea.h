@@ -108,6 +108,29 @@ int cea_attn_fwd(const cea_attn_params* p, void* stream);
 int cea_decode_splitkv(const cea_attn_params* p, void* stream);
 
 /*
+ * Split-KV decode that allocates nothing.  It has no counterpart in the
+ * reference: collab_infer's decode always allocates its partial results.
+ *
+ * Same parameters and result as cea_decode_splitkv, but p->workspace is
+ * ignored.  The per-split partials go to a fixed device array inside the
+ * library instead.  That array is CEA_NOALLOC_SCRATCH_BYTES on every GPU that
+ * loads libcea.so and is held until the process exits.  This entry point is
+ * meant for callers that only hold the input and output buffers and have no
+ * allocator to size a workspace from, such as a serving loop that reserves all
+ * its device memory at start-up and treats any later allocation as an error.
+ *
+ * The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  Calls share the array, so calls that overlap on
+ * the GPU (for example on two streams) race and must be ordered by the caller.
+ * The split count is reduced to fit the array.  A call whose single split of
+ * partials, B*Hq*Sq*(D+1)*4 bytes, exceeds it fails with CEA_ERR_WORKSPACE.
+ * It never calls cudaMalloc or cudaFree.
+ */
+#define CEA_NOALLOC_SCRATCH_BYTES (8u << 20)
+int cea_decode_splitkv_noalloc(const cea_attn_params* p, void* stream);
+
+/*
  * Exact merge of n partial attention results over disjoint key sets.
  * Replaces collab_infer parallel/attention.py:242-264 (merge_attention,
  * merge_attention_list).  Partial i is (outs[i], lses[i]); all partials share
