@@ -226,6 +226,32 @@ __global__ void tile_stats_kernel(const int64_t* pos, int64_t sb, int64_t ss, in
 }
 
 // ---------------------------------------------------------------------------
+// per query tile, the first and last key tile it can see (one warp per tile), so
+// the attention kernels do not scan the invisible causal future tile by tile
+// ---------------------------------------------------------------------------
+__global__ void tile_range_kernel(const TileStat* qstat, const TileStat* kstat, int nqt, int nkt, int B, int causal,
+                                  int2* range) {
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= B * nqt) return;
+  const int b = wid / nqt;
+  const TileStat qs = qstat[wid];
+  int first = nkt, last = -1;
+  for (int kt = lane; kt < nkt; kt += 32) {
+    if (classify(qs, kstat[static_cast<size_t>(b) * nkt + kt], causal != 0) != kSkip) {
+      first = kt < first ? kt : first;
+      last = kt > last ? kt : last;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    first = min(first, __shfl_xor_sync(0xffffffffu, first, off));
+    last = max(last, __shfl_xor_sync(0xffffffffu, last, off));
+  }
+  if (lane == 0) range[wid] = make_int2(first, last);
+}
+
+// ---------------------------------------------------------------------------
 // exact n-way merge of partial (out, lse) over disjoint key sets; one warp per row
 // ---------------------------------------------------------------------------
 struct MergeArgs {

@@ -70,6 +70,7 @@ struct Params {
   const int32_t* kv_map;
   const TileStat* qstat;  // [B][nqt]
   const TileStat* kstat;  // [B][nkt]
+  const int2* qrange;     // [B][nqt]: first and last key tile each query tile can see
   int B, Sq, Sk, Hq, Hkv, group, nqt, nkt;
   float scale_log2;
   int causal, out_dtype, accumulate;
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const TileStat qs = p.qstat[b * p.nqt + qt];
   const TileStat* kst = p.kstat + static_cast<size_t>(b) * p.nkt;
   const bool causal = p.causal != 0;
+  const int2 krange = p.qrange[b * p.nqt + qt];
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int kb = 0; kb < L::KBOX; ++kb)
         tma_load_4d(sbase + L::OFF_Q + kb * L::BOX, &tmQ, bar(L::B_QFULL), kb * 64, qt * BM, h, b);
       int it = 0;
-      for (int kt = 0; kt < p.nkt; ++kt) {
+      for (int kt = krange.x; kt <= krange.y; ++kt) {
         if (classify(qs, kst[kt], causal) == kSkip) continue;
         const int st = it % L::NSTAGE;
         const uint32_t n = it / L::NSTAGE;
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         return true;
       };
       int it = 0;
-      for (int kt = 0; ok && kt < p.nkt; ++kt) {
+      for (int kt = krange.x; ok && kt <= krange.y; ++kt) {
         if (classify(qs, kst[kt], causal) == kSkip) continue;
         const int st = it % L::NSTAGE;
         if (!mbar_wait(bar(L::B_KFULL + st), (it / L::NSTAGE) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) {
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float l = 0.f;        // running sum of exp2(s - m)
     int it = 0;
     bool ok = true;
-    for (int kt = 0; kt < p.nkt; ++kt) {
+    for (int kt = krange.x; kt <= krange.y; ++kt) {
       const int cls = classify(qs, kst[kt], causal);
       if (cls == kSkip) continue;
       if (!warp_wait(bar(L::B_SFULL + (it & 1)), (it >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
@@ -248,7 +250,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld32(tmem + (it & 1) * BN + c * 32 + lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
 
-      float tmax = -INFINITY;
+      // row max over the raw scores (the scale is positive, so it commutes with max); invisible keys
+      // become -inf in place.  Eight independent accumulators keep the dependency chains short.
+      float mx[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
       if (cls == kMasked) {
         const int kbase = kt * BN;
 #pragma unroll
@@ -256,18 +262,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int key = kbase + j;
           const long long kp = key < p.Sk ? kpos_b[static_cast<int64_t>(key) * p.kpos_ss] : -1ll;
           const bool vis = kp >= 0 && (!causal || kp <= qpos);
-          const float v = vis ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
-          s[j] = __float_as_uint(v);
-          tmax = fmaxf(tmax, v);
+          if (!vis) s[j] = __float_as_uint(-INFINITY);
+          mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(s[j]));
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < BN; ++j) {
-          const float v = __uint_as_float(s[j]) * p.scale_log2;
-          s[j] = __float_as_uint(v);
-          tmax = fmaxf(tmax, v);
-        }
+        for (int j = 0; j < BN; ++j) mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(s[j]));
       }
+      const float tmax =
+          fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+          p.scale_log2;
       const float m_new = fmaxf(m, tmax);
       const bool rescale = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
       float alpha = 1.f;
@@ -278,7 +282,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         l *= alpha;
         m = m_new;
       }
-      const float m_use = (m == -INFINITY) ? 0.f : m;
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
 
       // P(it) goes into buffer it&1, last read by PV(it-2)
       if (it >= 2 &&
@@ -287,20 +291,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       uint8_t* prow = smem + L::OFF_P + (it & 1) * L::PTILE + row * 128;
-      float rowsum = 0.f;
+      float rs[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) rs[a] = 0.f;
+      const bool poly_ok = cls == kFull;  // no -inf arguments: part of the exponentials may go to the FMA pipe
 #pragma unroll
       for (int c = 0; c < BN / 8; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(__uint_as_float(s[c * 8 + 2 * e]) - m_use);
-          const float p1 = fast_exp2(__uint_as_float(s[c * 8 + 2 * e + 1]) - m_use);
-          rowsum += p0 + p1;
+          const float x0 = fmaf(__uint_as_float(s[c * 8 + 2 * e]), p.scale_log2, neg_m);
+          const float x1 = fmaf(__uint_as_float(s[c * 8 + 2 * e + 1]), p.scale_log2, neg_m);
+          // elements 5, 6, 7 of every 8 on the FMA pipe when the tile is fully visible
+          const float p0 = (poly_ok && 2 * e >= 5) ? exp2_poly3(x0) : fast_exp2(x0);
+          const float p1 = (poly_ok && 2 * e + 1 >= 5) ? exp2_poly3(x1) : fast_exp2(x1);
+          rs[2 * e] += p0;
+          rs[2 * e + 1] += p1;
           w[e] = pack2(p0, p1, kBF16);
         }
         const int chunk = (c & 7) ^ (row & 7);
         *reinterpret_cast<uint4*>(prow + (c >> 3) * L::BOX + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
       }
+      const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
       l += rowsum;
 
       if (__any_sync(0xffffffffu, rescale)) {

@@ -85,21 +85,6 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
-// 2^x for x <= 0 on the FMA pipe: x = n + f, n = round(x), f in [-0.5, 0.5];
-// 2^f ~ c0 + f (c1 + f (c2 + f c3)) (least-squares fit, max rel. err 7.5e-5);
-// 2^n applied by adding n to the exponent field.  x is clamped at -125 so the
-// exponent cannot underflow (2^-125 is below anything that matters here).
-__device__ __forceinline__ float exp2_poly3(float x) {
-  const float xc = fmaxf(x, -125.0f);
-  const float t = xc + 12582912.0f;  // 1.5 * 2^23: the integer part lands in the low mantissa bits
-  const float n = t - 12582912.0f;
-  const float f = xc - n;
-  float p = fmaf(0.055171623826026917f, f, 0.2426111251115799f);
-  p = fmaf(p, f, 0.6932609677314758f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 template <int D, bool kBF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -148,6 +133,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const TileStat qs1 = active[1] ? p.qstat[b * p.nqt + qt[1]] : TileStat{LLONG_MAX, -1, 0, 0};
   const TileStat* kst = p.kstat + static_cast<size_t>(b) * p.nkt;
   const bool causal = p.causal != 0;
+  int2 krange = p.qrange[b * p.nqt + qt[0]];
+  if (active[1]) {
+    const int2 r1 = p.qrange[b * p.nqt + qt[1]];
+    krange = make_int2(min(krange.x, r1.x), max(krange.y, r1.y));
+  }
   auto cls_of = [&](int h, int kt) -> int {
     if (!active[h]) return kSkip;
     return classify(h == 0 ? qs0 : qs1, kst[kt], causal);
@@ -199,7 +189,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                       head[h], b);
       }
       int u = 0;
-      for (int kt = 0; kt < p.nkt; ++kt) {
+      for (int kt = krange.x; kt <= krange.y; ++kt) {
         if (cls_of(0, kt) == kSkip && cls_of(1, kt) == kSkip) continue;
         const int ks = u % L::KST, vs = u % L::VST;
         const uint32_t kn = u / L::KST, vn = u / L::VST;
@@ -250,7 +240,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         return true;
       };
       int u = 0;
-      for (int kt = 0; ok && kt < p.nkt; ++kt) {
+      for (int kt = krange.x; ok && kt <= krange.y; ++kt) {
         const int c0 = cls_of(0, kt), c1 = cls_of(1, kt);
         if (c0 == kSkip && c1 == kSkip) continue;
         const int ks = u % L::KST;
@@ -305,7 +295,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int it = 0;
     bool ok = true;
     if (active[h]) {
-      for (int kt = 0; kt < p.nkt; ++kt) {
+      for (int kt = krange.x; kt <= krange.y; ++kt) {
         const int cls = cls_of(h, kt);
         if (cls == kSkip) continue;
         if (!tc::warp_wait(bar(L::B_SFULL + h), it & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {

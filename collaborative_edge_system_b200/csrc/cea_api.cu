@@ -194,7 +194,8 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 size_t tc_stats_bytes(const cea_attn_params* p) {
   const int nqt = (p->Sq + tc::BM - 1) / tc::BM, nkt = (p->Sk + tc::BN - 1) / tc::BN;
-  return align256(static_cast<size_t>(p->B) * (nqt + nkt) * sizeof(TileStat));
+  return align256(static_cast<size_t>(p->B) * (nqt + nkt) * sizeof(TileStat)) +
+         align256(static_cast<size_t>(p->B) * nqt * sizeof(int2));
 }
 
 template <typename K>
@@ -242,6 +243,8 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   const int nqt = (p->Sq + tc::BM - 1) / tc::BM, nkt = (p->Sk + tc::BN - 1) / tc::BN;
   TileStat* qstat = reinterpret_cast<TileStat*>(p->workspace);
   TileStat* kstat = qstat + static_cast<size_t>(p->B) * nqt;
+  int2* qrange = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(p->workspace) +
+                                         align256(static_cast<size_t>(p->B) * (nqt + nkt) * sizeof(TileStat)));
   {
     const int warps = p->B * (nqt + nkt);
     (void)warps;
@@ -250,6 +253,7 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
                                                    0, qstat);
     tile_stats_kernel<<<(wk + 3) / 4, 128, 0, s>>>(p->k_pos, p->kpos_stride[0], p->kpos_stride[1], p->Sk, nkt, p->B,
                                                    1, kstat);
+    tile_range_kernel<<<(wq + 3) / 4, 128, 0, s>>>(qstat, kstat, nqt, nkt, p->B, p->causal, qrange);
     if (int e = cuda_check("tile_stats_kernel")) return e;
   }
   CUtensorMap mq, mk, mv;
@@ -275,6 +279,7 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   tp.kv_map = p->kv_map;
   tp.qstat = qstat;
   tp.kstat = kstat;
+  tp.qrange = qrange;
   tp.B = p->B;
   tp.Sq = p->Sq;
   tp.Sk = p->Sk;
