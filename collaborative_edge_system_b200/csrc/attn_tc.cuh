@@ -18,6 +18,8 @@
 // ones skip the element mask.
 #pragma once
 
+#include <type_traits>
+
 #include "cea_common.cuh"
 
 namespace cea {
@@ -31,6 +33,12 @@ constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only when the max grows by > 256x
+
+// 1: part of the exponentials of fully visible tiles run on the FMA pipe (exp2_poly3); off by
+// default: measured slower here because the softmax is latency- rather than MUFU-bound
+#ifndef CEA_POLY_EXP2
+#define CEA_POLY_EXP2 0
+#endif
 
 template <int D>
 struct Layout {
@@ -294,23 +302,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       float rs[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) rs[a] = 0.f;
-      const bool poly_ok = cls == kFull;  // no -inf arguments: part of the exponentials may go to the FMA pipe
+      // P row = 2^(s*scale - m) as 16-bit pairs, stored 8 keys (16 B) at a time into the swizzled tile.
+      // On fully visible tiles (no -inf arguments) elements 5, 6, 7 of every 8 use the FMA pipe.
+      auto emit = [&](auto use_poly) {
 #pragma unroll
-      for (int c = 0; c < BN / 8; ++c) {
-        uint32_t w[4];
+        for (int c = 0; c < BN / 8; ++c) {
+          uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x0 = fmaf(__uint_as_float(s[c * 8 + 2 * e]), p.scale_log2, neg_m);
-          const float x1 = fmaf(__uint_as_float(s[c * 8 + 2 * e + 1]), p.scale_log2, neg_m);
-          // elements 5, 6, 7 of every 8 on the FMA pipe when the tile is fully visible
-          const float p0 = (poly_ok && 2 * e >= 5) ? exp2_poly3(x0) : fast_exp2(x0);
-          const float p1 = (poly_ok && 2 * e + 1 >= 5) ? exp2_poly3(x1) : fast_exp2(x1);
-          rs[2 * e] += p0;
-          rs[2 * e + 1] += p1;
-          w[e] = pack2(p0, p1, kBF16);
+          for (int e = 0; e < 4; ++e) {
+            const float x0 = fmaf(__uint_as_float(s[c * 8 + 2 * e]), p.scale_log2, neg_m);
+            const float x1 = fmaf(__uint_as_float(s[c * 8 + 2 * e + 1]), p.scale_log2, neg_m);
+            const float p0 = (decltype(use_poly)::value && 2 * e >= 5) ? exp2_poly3(x0) : fast_exp2(x0);
+            const float p1 = (decltype(use_poly)::value && 2 * e + 1 >= 5) ? exp2_poly3(x1) : fast_exp2(x1);
+            rs[2 * e] += p0;
+            rs[2 * e + 1] += p1;
+            w[e] = pack2(p0, p1, kBF16);
+          }
+          const int chunk = (c & 7) ^ (row & 7);
+          *reinterpret_cast<uint4*>(prow + (c >> 3) * L::BOX + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        const int chunk = (c & 7) ^ (row & 7);
-        *reinterpret_cast<uint4*>(prow + (c >> 3) * L::BOX + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      };
+      if (CEA_POLY_EXP2 && cls == kFull) {
+        emit(std::true_type{});
+      } else {
+        emit(std::false_type{});
       }
       const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
       l += rowsum;
