@@ -2,15 +2,20 @@
 //
 // One CTA computes a 128-query tile of one (batch, query head) against every
 // visible 128-key tile of its KV head:
-//   warp 4      TMA producer: Q once, then K and V tiles into an NSTAGE ring
-//   warp 5      MMA issuer (one thread): S = Q K^T into TMEM (double-buffered),
-//               O += P V into a TMEM accumulator; completion via tcgen05.commit
-//   warps 0-3   softmax: one thread per query row (= TMEM lane); reads S from
-//               TMEM, applies the position mask, keeps the running max/sum in
-//               fp32 (log2 domain), writes P (bf16/fp16) into shared memory in
-//               the 128B-swizzled K-major operand layout, rescales O in TMEM when
-//               the running max grows by more than 2^8, and finally normalises O,
-//               writes out/lse and (accumulate mode) merges into the stored result.
+//   warp 8       TMA producer: Q once, then K and V tiles into an NSTAGE ring
+//   warp 9       MMA issuer (one thread): S(t) = Q K(t)^T into TMEM buffer t&1,
+//                O_{t&1} += P(t) V(t); completion via tcgen05.commit
+//   warps 0-3    softmax of the even key tiles, warps 4-7 of the odd ones:
+//                one thread per query row (= TMEM lane) reads S from TMEM,
+//                applies the position mask, keeps its own running max/sum in
+//                fp32 (log2 domain), writes P (bf16/fp16) into shared memory in
+//                the 128B-swizzled K-major operand layout and rescales its own O
+//                accumulator in TMEM when its max grows by more than 2^8
+//   warps 10-11  idle (they complete the third warpgroup for setmaxnreg)
+// Two softmax warpgroups keep the MUFU pipe busy while the other one waits,
+// reduces or stores; each owns an O accumulator (TMEM: S0, S1, O0, O1 = 512
+// columns), and the epilogue merges the two partial results exactly, writes
+// out/lse and, in accumulate mode, merges into the stored (out, lse).
 //
 // Tile skipping and masking follow per-tile position statistics computed by
 // tile_stats_kernel, so any token layout (contiguous, zigzag, padded, uneven)
@@ -27,10 +32,12 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int NUM_THREADS = 192;
-constexpr int kSoftmaxWarps = 4;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int NUM_THREADS = 384;
+constexpr int kSoftmaxWarps = 8;  // two warpgroups
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kRegsSoftmax = 232;  // setmaxnreg split: 232 + 232 + 40 per SMSP (launch reserves 3 x 168)
+constexpr uint32_t kRegsOther = 40;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only when the max grows by > 256x
 
@@ -127,7 +134,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(L::B_SFULL + s), 1);
-      mbar_init(bar(L::B_PFULL + s), kSoftmaxWarps * 32);
+      mbar_init(bar(L::B_PFULL + s), 128);  // the warpgroup that owns tiles of parity s
       mbar_init(bar(L::B_PVDONE + s), 1);
     }
     *abort_flag = 0;
@@ -152,6 +159,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const bool causal = p.causal != 0;
   const int2 krange = p.qrange[b * p.nqt + qt];
 
+  if (warp >= kProducerWarp) {
+    // ================================================================ warpgroup 2
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -184,7 +194,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t kIdescQK = idesc_f16(kBF16, false, BM, BN);
       constexpr uint32_t kIdescPV = idesc_f16(kBF16, true, BM, D);
-      const uint32_t tO = tmem + 256;
       bool ok = mbar_wait(bar(L::B_QFULL), 0, abort_flag, CEA_DEV_TIMEOUT_MMA);
       // O += P(j) V(j): P from shared memory (K-major over keys), V MN-major (D contiguous)
       auto issue_pv = [&](int j) -> bool {
@@ -194,11 +203,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t pbase = sbase + L::OFF_P + (j & 1) * L::PTILE;
         const uint32_t vbase = sbase + L::OFF_V + st * L::TILE;
+        const uint32_t tO = tmem + 256 + (j & 1) * 128;  // the accumulator of the warpgroup that owns tile j
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t a = sw128_desc(pbase + (kk >> 2) * L::BOX + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(vbase + kk * 16 * 128, L::BOX, 1024);
-          umma_ss(tO, a, bd, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_ss(tO, a, bd, kIdescPV, (j >= 2 || kk > 0) ? 1u : 0u);
         }
         umma_commit(bar(L::B_VEMPTY + st));
         umma_commit(bar(L::B_PVDONE + (j & 1)));
@@ -232,30 +242,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (ok && it > 0) issue_pv(it - 1);
     }
+  }
   } else {
-    // ------------------------------------------------------------ softmax + epilogue
-    const int row = threadIdx.x;  // TMEM lane == query row within the tile
+    // ================================================================ warpgroups 0, 1: softmax + epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+    const int wg = warp >> 2;        // owns the key tiles t with t % 2 == wg
+    const int row = threadIdx.x & 127;  // TMEM lane == query row within the tile
     const int q_row = qt * BM + row;
     const bool row_in = q_row < p.Sq;
     const long long qpos = row_in ? p.q_pos[b * p.qpos_sb + static_cast<int64_t>(q_row) * p.qpos_ss] : -1ll;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + wg * BN + lane_base;
+    const uint32_t tO = tmem + 256 + wg * 128 + lane_base;
     const int64_t* kpos_b = p.k_pos + b * p.kpos_sb;
     float m = -INFINITY;  // running max actually used as the exponent offset (log2 domain)
     float l = 0.f;        // running sum of exp2(s - m)
-    int it = 0;
+    int it = 0;           // key tiles processed by the CTA (both warpgroups)
     bool ok = true;
     for (int kt = krange.x; kt <= krange.y; ++kt) {
       const int cls = classify(qs, kst[kt], causal);
       if (cls == kSkip) continue;
-      if (!warp_wait(bar(L::B_SFULL + (it & 1)), (it >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
+      if ((it & 1) != wg) {
+        ++it;
+        continue;
+      }
+      if (!warp_wait(bar(L::B_SFULL + wg), (it >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t s[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        tmem_ld32(tmem + (it & 1) * BN + c * 32 + lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
 
       // row max over the raw scores (the scale is positive, so it commutes with max); invisible keys
@@ -264,13 +282,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
       if (cls == kMasked) {
-        const int kbase = kt * BN;
+        // visibility of the tile's keys, 32 at a time (bounds the registers holding positions)
+        uint32_t vis[BN / 32];
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t bits = 0u;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = kt * BN + c * 32 + e;
+            const long long kp = key < p.Sk ? kpos_b[static_cast<int64_t>(key) * p.kpos_ss] : -1ll;
+            bits |= (kp >= 0 && (!causal || kp <= qpos)) ? (1u << e) : 0u;
+          }
+          vis[c] = bits;
+        }
 #pragma unroll
         for (int j = 0; j < BN; ++j) {
-          const int key = kbase + j;
-          const long long kp = key < p.Sk ? kpos_b[static_cast<int64_t>(key) * p.kpos_ss] : -1ll;
-          const bool vis = kp >= 0 && (!causal || kp <= qpos);
-          if (!vis) s[j] = __float_as_uint(-INFINITY);
+          if (!((vis[j >> 5] >> (j & 31)) & 1u)) s[j] = __float_as_uint(-INFINITY);
           mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(s[j]));
         }
       } else {
@@ -284,7 +311,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool rescale = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
       float alpha = 1.f;
       if (m == -INFINITY) {
-        m = m_new;  // first visible key of this row: O and l are still zero
+        m = m_new;  // first visible key of this row for this warpgroup: its O and l are still zero
       } else if (rescale) {
         alpha = fast_exp2(m - m_new);
         l *= alpha;
@@ -292,18 +319,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
 
-      // P(it) goes into buffer it&1, last read by PV(it-2)
-      if (it >= 2 &&
-          !warp_wait(bar(L::B_PVDONE + (it & 1)), ((it - 2) >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
+      // P(it) goes into buffer wg, last read by PV(it-2); PV(it-2) is also the latest product in O_wg
+      if (it >= 2 && !warp_wait(bar(L::B_PVDONE + wg), ((it - 2) >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
         ok = false;
         break;
       }
-      uint8_t* prow = smem + L::OFF_P + (it & 1) * L::PTILE + row * 128;
+      uint8_t* prow = smem + L::OFF_P + wg * L::PTILE + row * 128;
       float rs[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) rs[a] = 0.f;
       // P row = 2^(s*scale - m) as 16-bit pairs, stored 8 keys (16 B) at a time into the swizzled tile.
-      // On fully visible tiles (no -inf arguments) elements 5, 6, 7 of every 8 use the FMA pipe.
+      // On fully visible tiles (no -inf arguments) elements 5, 6, 7 of every 8 may use the FMA pipe.
       auto emit = [&](auto use_poly) {
 #pragma unroll
         for (int c = 0; c < BN / 8; ++c) {
@@ -331,95 +357,107 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       l += rowsum;
 
       if (__any_sync(0xffffffffu, rescale)) {
-        // O holds PV(0..it-1); wait for PV(it-1) before scaling it in place
-        if (!warp_wait(bar(L::B_PVDONE + ((it - 1) & 1)), ((it - 1) >> 1) & 1, abort_flag,
-                       CEA_DEV_TIMEOUT_SOFTMAX)) {
-          ok = false;
-          break;
-        }
+        // O_wg holds PV(wg), PV(wg+2), ..., PV(it-2), all complete (waited above)
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
-          tmem_ld32(tmem + 256 + c * 32 + lane_base, o);
+          tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tmem + 256 + c * 32 + lane_base, o);
+          tmem_st32(tO + c * 32, o);
         }
         tmem_wait_st();
       }
       fence_async_smem();  // P stores -> visible to the tensor-core (async) proxy
       tc_fence_before();
-      mbar_arrive(bar(L::B_PFULL + (it & 1)));
+      mbar_arrive(bar(L::B_PFULL + wg));
       ++it;
     }
 
     // --------------------------------------------------------------- epilogue
-    if (ok && it > 0) {
-      ok = warp_wait(bar(L::B_PVDONE + ((it - 1) & 1)), ((it - 1) >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
+    // `it` is now the number of processed tiles N for both warpgroups.  PV(N-1) is the last
+    // tcgen05 operation of the CTA: once it completes, every S (which reads Q) and PV has.
+    const int N = it;
+    if (ok && N > 0) {
+      ok = warp_wait(bar(L::B_PVDONE + ((N - 1) & 1)), ((N - 1) >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
       tc_fence_after();
     }
-    if (ok && !(it == 0 && p.accumulate)) {
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      const float lse_row = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
+    // the two warpgroups exchange (m, l) through the dead Q tile and merge exactly
+    float2* ml = reinterpret_cast<float2*>(smem + L::OFF_Q);
+    float* lse_ptr = p.lse ? p.lse + b * p.l_sb + h * p.l_sh + static_cast<int64_t>(q_row) * p.l_ss : nullptr;
+    const float lse_old = (ok && p.accumulate && row_in) ? *lse_ptr : -INFINITY;  // read before anyone writes
+    if (ok) ml[wg * 128 + row] = make_float2(m, l);
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const bool all_ok = ok && !*abort_flag;
+    if (all_ok && !(N == 0 && p.accumulate)) {
+      const float2 mine = ml[wg * 128 + row], other = ml[(wg ^ 1) * 128 + row];
+      const float m0 = wg == 0 ? mine.x : other.x, l0 = wg == 0 ? mine.y : other.y;
+      const float m1 = wg == 0 ? other.x : mine.x, l1 = wg == 0 ? other.y : mine.y;
+      const float M = fmaxf(l0 > 0.f ? m0 : -INFINITY, l1 > 0.f ? m1 : -INFINITY);
+      const float a0 = l0 > 0.f ? fast_exp2(m0 - M) : 0.f;
+      const float a1 = l1 > 0.f ? fast_exp2(m1 - M) : 0.f;
+      const float L = l0 * a0 + l1 * a1;
+      const float inv_l = L > 0.f ? 1.f / L : 0.f;
+      const float lse_row = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
       float w_old = 0.f, w_new = 1.f, lse_out = lse_row;
-      float* lse_ptr = p.lse ? p.lse + b * p.l_sb + h * p.l_sh + static_cast<int64_t>(q_row) * p.l_ss : nullptr;
       if (p.accumulate && row_in) {
-        const float lse_old = *lse_ptr;
-        const float mx = fmaxf(lse_old, lse_row);
-        if (mx == -INFINITY) {
+        const float mxl = fmaxf(lse_old, lse_row);
+        if (mxl == -INFINITY) {
           lse_out = -INFINITY;
           w_old = 0.f;
           w_new = 0.f;
         } else {
-          lse_out = mx + log1pf(expf(-fabsf(lse_old - lse_row)));
+          lse_out = mxl + log1pf(expf(-fabsf(lse_old - lse_row)));
           w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - lse_out);
           w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - lse_out);
         }
       }
-      const float scale_new = inv_l * w_new;
+      const float c0 = a0 * inv_l * w_new, c1 = a1 * inv_l * w_new;
+      const bool has0 = N >= 1, has1 = N >= 2;  // accumulators that received at least one PV
+      const uint32_t tO0 = tmem + 256 + lane_base, tO1 = tmem + 384 + lane_base;
       const int64_t obase = b * p.o_sb + static_cast<int64_t>(q_row) * p.o_ss + h * p.o_sh;
+      // each warpgroup finishes half of the columns, 16 at a time
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        if (it > 0) {
-          tmem_ld32(tmem + 256 + c * 32 + lane_base, o);
-          tmem_wait_ld();
-        } else {
+      for (int c = wg * (D / 32); c < (wg + 1) * (D / 32); ++c) {
+        uint32_t o0[16], o1[16];
+        if (has0) tmem_ld16(tO0 + c * 16, o0);
+        if (has1) tmem_ld16(tO1 + c * 16, o1);
+        tmem_wait_ld();
+        float v[16];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0u;
-        }
+        for (int e = 0; e < 16; ++e)
+          v[e] = (has0 ? __uint_as_float(o0[e]) * c0 : 0.f) + (has1 ? __uint_as_float(o1[e]) * c1 : 0.f);
         if (!row_in) continue;
         if (p.out_dtype == CEA_F32) {
-          float* dst = reinterpret_cast<float*>(p.out) + obase + c * 32;
+          float* dst = reinterpret_cast<float*>(p.out) + obase + c * 16;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float4 v = make_float4(__uint_as_float(o[e]) * scale_new, __uint_as_float(o[e + 1]) * scale_new,
-                                   __uint_as_float(o[e + 2]) * scale_new, __uint_as_float(o[e + 3]) * scale_new);
+          for (int e = 0; e < 16; e += 4) {
+            float4 x = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
             if (p.accumulate) {
               const float4 old = *reinterpret_cast<const float4*>(dst + e);
-              v.x += old.x * w_old;
-              v.y += old.y * w_old;
-              v.z += old.z * w_old;
-              v.w += old.w * w_old;
+              x.x += old.x * w_old;
+              x.y += old.y * w_old;
+              x.z += old.z * w_old;
+              x.w += old.w * w_old;
             }
-            *reinterpret_cast<float4*>(dst + e) = v;
+            *reinterpret_cast<float4*>(dst + e) = x;
           }
         } else {
-          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + obase + c * 32;
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + obase + c * 16;
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 v;
-            v.x = pack2(__uint_as_float(o[e]) * scale_new, __uint_as_float(o[e + 1]) * scale_new, kBF16);
-            v.y = pack2(__uint_as_float(o[e + 2]) * scale_new, __uint_as_float(o[e + 3]) * scale_new, kBF16);
-            v.z = pack2(__uint_as_float(o[e + 4]) * scale_new, __uint_as_float(o[e + 5]) * scale_new, kBF16);
-            v.w = pack2(__uint_as_float(o[e + 6]) * scale_new, __uint_as_float(o[e + 7]) * scale_new, kBF16);
-            *reinterpret_cast<uint4*>(dst + e) = v;
+          for (int e = 0; e < 16; e += 8) {
+            uint4 x;
+            x.x = pack2(v[e], v[e + 1], kBF16);
+            x.y = pack2(v[e + 2], v[e + 3], kBF16);
+            x.z = pack2(v[e + 4], v[e + 5], kBF16);
+            x.w = pack2(v[e + 6], v[e + 7], kBF16);
+            *reinterpret_cast<uint4*>(dst + e) = x;
           }
         }
       }
-      if (row_in && lse_ptr) *lse_ptr = lse_out;
+      if (wg == 0 && row_in && lse_ptr) *lse_ptr = lse_out;
     }
   }
 
