@@ -377,17 +377,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
 
     // --------------------------------------------------------------- epilogue
-    // `it` is now the number of processed tiles N for both warpgroups.  PV(N-1) is the last
-    // tcgen05 operation of the CTA: once it completes, every S (which reads Q) and PV has.
+    // `it` is now the number of processed tiles N for both warpgroups.  Each warpgroup waits for
+    // its own last PV on its own pv_done barrier: it has followed that barrier phase by phase, so
+    // the parity wait cannot be satisfied by an older phase (the other warpgroup's barrier could be
+    // two phases behind, where a parity wait returns at once).  After the named barrier both last
+    // PVs, and with them every tcgen05 operation of the CTA (they complete in issue order), are done.
     const int N = it;
-    if (ok && N > 0) {
-      ok = warp_wait(bar(L::B_PVDONE + ((N - 1) & 1)), ((N - 1) >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
+    const int n_mine = (N - wg + 1) / 2;  // tiles wg, wg+2, ... below N
+    if (ok && n_mine > 0) {
+      ok = warp_wait(bar(L::B_PVDONE + wg), (n_mine - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
       tc_fence_after();
     }
-    // the two warpgroups exchange (m, l) through the dead Q tile and merge exactly
-    float2* ml = reinterpret_cast<float2*>(smem + L::OFF_Q);
     float* lse_ptr = p.lse ? p.lse + b * p.l_sb + h * p.l_sh + static_cast<int64_t>(q_row) * p.l_ss : nullptr;
     const float lse_old = (ok && p.accumulate && row_in) ? *lse_ptr : -INFINITY;  // read before anyone writes
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    tc_fence_after();
+    // the Q tile is dead now: the two warpgroups exchange (m, l) through it and merge exactly
+    float2* ml = reinterpret_cast<float2*>(smem + L::OFF_Q);
     if (ok) ml[wg * 128 + row] = make_float2(m, l);
     asm volatile("bar.sync 1, 256;" ::: "memory");
     const bool all_ok = ok && !*abort_flag;
