@@ -2,16 +2,16 @@
 //
 // One CTA computes a 128-query tile of one (batch, query head) against every
 // visible 128-key tile of its KV head:
-//   warp 8       TMA producer: Q once, then K and V tiles into an NSTAGE ring
-//   warp 9       MMA issuer (one thread): S(t) = Q K(t)^T into TMEM buffer t&1,
-//                O_{t&1} += P(t) V(t); completion via tcgen05.commit
+//   warps 8, 10  TMA producers: Q once and the K ring (warp 8), the V ring (warp 10)
+//   warp 9       MMA issuer (one thread, event driven): S(t) = Q K(t)^T into TMEM
+//                buffer t&1, O_{t&1} += P(t) V(t); completion via tcgen05.commit
 //   warps 0-3    softmax of the even key tiles, warps 4-7 of the odd ones:
 //                one thread per query row (= TMEM lane) reads S from TMEM,
 //                applies the position mask, keeps its own running max/sum in
 //                fp32 (log2 domain), writes P (bf16/fp16) into shared memory in
 //                the 128B-swizzled K-major operand layout and rescales its own O
 //                accumulator in TMEM when its max grows by more than 2^8
-//   warps 10-11  idle (they complete the third warpgroup for setmaxnreg)
+//   warp 11      idle (it completes the third warpgroup for setmaxnreg)
 // Two softmax warpgroups keep the MUFU pipe busy while the other one waits,
 // reduces or stores; each owns an O accumulator (TMEM: S0, S1, O0, O1 = 512
 // columns), and the epilogue merges the two partial results exactly, writes
@@ -34,8 +34,9 @@ constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int NUM_THREADS = 384;
 constexpr int kSoftmaxWarps = 8;  // two warpgroups
-constexpr int kProducerWarp = 8;
+constexpr int kProducerWarp = 8;   // Q and K tiles
 constexpr int kMmaWarp = 9;
+constexpr int kVProducerWarp = 10;  // V tiles
 constexpr uint32_t kRegsSoftmax = 232;  // setmaxnreg split: 232 + 232 + 40 per SMSP (launch reserves 3 x 168)
 constexpr uint32_t kRegsOther = 40;
 constexpr uint32_t kTmemCols = 512;
@@ -162,87 +163,109 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp >= kProducerWarp) {
     // ================================================================ warpgroup 2
     asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(bar(L::B_QFULL), L::TILE);
+    if ((warp == kProducerWarp || warp == kVProducerWarp) && lane == 0) {
+      // ---------------------------------------------------------- TMA producers: Q and the K ring
+      // (warp 8), the V ring (warp 10); independent, so a K tile never waits behind a V stage
+      const bool is_k = warp == kProducerWarp;
+      if (is_k) {
+        mbar_arrive_expect_tx(bar(L::B_QFULL), L::TILE);
 #pragma unroll
-      for (int kb = 0; kb < L::KBOX; ++kb)
-        tma_load_4d(sbase + L::OFF_Q + kb * L::BOX, &tmQ, bar(L::B_QFULL), kb * 64, qt * BM, h, b);
+        for (int kb = 0; kb < L::KBOX; ++kb)
+          tma_load_4d(sbase + L::OFF_Q + kb * L::BOX, &tmQ, bar(L::B_QFULL), kb * 64, qt * BM, h, b);
+      }
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      const int off = is_k ? L::OFF_K : L::OFF_V;
+      const int b_full = is_k ? L::B_KFULL : L::B_VFULL;
+      const int b_empty = is_k ? L::B_KEMPTY : L::B_VEMPTY;
       int it = 0;
       for (int kt = krange.x; kt <= krange.y; ++kt) {
         if (classify(qs, kst[kt], causal) == kSkip) continue;
         const int st = it % L::NSTAGE;
         const uint32_t n = it / L::NSTAGE;
-        if (n > 0 && !mbar_wait(bar(L::B_KEMPTY + st), (n - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(bar(L::B_KFULL + st), L::TILE);
+        if (n > 0 && !mbar_wait(bar(b_empty + st), (n - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(bar(b_full + st), L::TILE);
 #pragma unroll
         for (int kb = 0; kb < L::KBOX; ++kb)
-          tma_load_4d(sbase + L::OFF_K + st * L::TILE + kb * L::BOX, &tmK, bar(L::B_KFULL + st), kb * 64, kt * BN,
-                      kvh, b);
-        if (n > 0 && !mbar_wait(bar(L::B_VEMPTY + st), (n - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(bar(L::B_VFULL + st), L::TILE);
-#pragma unroll
-        for (int kb = 0; kb < L::KBOX; ++kb)
-          tma_load_4d(sbase + L::OFF_V + st * L::TILE + kb * L::BOX, &tmV, bar(L::B_VFULL + st), kb * 64, kt * BN,
-                      kvh, b);
+          tma_load_4d(sbase + off + st * L::TILE + kb * L::BOX, map, bar(b_full + st), kb * 64, kt * BN, kvh, b);
         ++it;
       }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    } else if (warp == kMmaWarp && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer (one thread)
+      // Event driven: S(t) goes out as soon as K(t) has landed and softmax(t-2) has released
+      // S buffer t&1; PV(t) as soon as P(t) and V(t) are ready.  p_full completions are observed
+      // strictly in order per buffer (`seen`), so a parity test never aliases an older phase.
       constexpr uint32_t kIdescQK = idesc_f16(kBF16, false, BM, BN);
       constexpr uint32_t kIdescPV = idesc_f16(kBF16, true, BM, D);
       bool ok = mbar_wait(bar(L::B_QFULL), 0, abort_flag, CEA_DEV_TIMEOUT_MMA);
-      // O += P(j) V(j): P from shared memory (K-major over keys), V MN-major (D contiguous)
-      auto issue_pv = [&](int j) -> bool {
-        const int st = j % L::NSTAGE;
-        if (!mbar_wait(bar(L::B_PFULL + (j & 1)), (j >> 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(bar(L::B_VFULL + st), (j / L::NSTAGE) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) return false;
-        tc_fence_after();
-        const uint32_t pbase = sbase + L::OFF_P + (j & 1) * L::PTILE;
-        const uint32_t vbase = sbase + L::OFF_V + st * L::TILE;
-        const uint32_t tO = tmem + 256 + (j & 1) * 128;  // the accumulator of the warpgroup that owns tile j
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = sw128_desc(pbase + (kk >> 2) * L::BOX + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(vbase + kk * 16 * 128, L::BOX, 1024);
-          umma_ss(tO, a, bd, kIdescPV, (j >= 2 || kk > 0) ? 1u : 0u);
+      int it_s = 0, it_pv = 0;  // next S and next PV, in processed-tile order
+      int seen[2] = {0, 0};     // p_full completions observed, per buffer
+      int kt = krange.x;        // key tile of S(it_s)
+      while (kt <= krange.y && classify(qs, kst[kt], causal) == kSkip) ++kt;
+      auto p_ready = [&](int t) -> bool {
+        const int bb = t & 1, idx = t >> 1;
+        if (seen[bb] > idx) return true;
+        if (mbar_test(bar(L::B_PFULL + bb), idx & 1)) {
+          seen[bb] = idx + 1;
+          return true;
         }
-        umma_commit(bar(L::B_VEMPTY + st));
-        umma_commit(bar(L::B_PVDONE + (j & 1)));
-        return true;
+        return false;
       };
-      int it = 0;
-      for (int kt = krange.x; ok && kt <= krange.y; ++kt) {
-        if (classify(qs, kst[kt], causal) == kSkip) continue;
-        const int st = it % L::NSTAGE;
-        if (!mbar_wait(bar(L::B_KFULL + st), (it / L::NSTAGE) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // S(it) = Q K^T into the TMEM buffer it&1 (free: softmax(it-2) handed over P(it-2))
-        const uint32_t tS = tmem + (it & 1) * BN;
-        const uint32_t kbase = sbase + L::OFF_K + st * L::TILE;
+      uint64_t t_prog = global_timer_ns();
+      while (ok && (kt <= krange.y || it_pv < it_s)) {
+        bool progress = false;
+        if (kt <= krange.y) {
+          const int st = it_s % L::NSTAGE;
+          if ((it_s < 2 || p_ready(it_s - 2)) && mbar_test(bar(L::B_KFULL + st), (it_s / L::NSTAGE) & 1)) {
+            tc_fence_after();
+            const uint32_t tS = tmem + (it_s & 1) * BN;
+            const uint32_t kbase = sbase + L::OFF_K + st * L::TILE;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
-          umma_ss(tS, sw128_desc(sbase + L::OFF_Q + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), kIdescQK,
-                  kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
+              umma_ss(tS, sw128_desc(sbase + L::OFF_Q + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), kIdescQK,
+                      kk > 0 ? 1u : 0u);
+            }
+            umma_commit(bar(L::B_SFULL + (it_s & 1)));
+            umma_commit(bar(L::B_KEMPTY + st));
+            ++it_s;
+            ++kt;
+            while (kt <= krange.y && classify(qs, kst[kt], causal) == kSkip) ++kt;
+            progress = true;
+          }
         }
-        umma_commit(bar(L::B_SFULL + (it & 1)));
-        umma_commit(bar(L::B_KEMPTY + st));
-        if (it > 0 && !issue_pv(it - 1)) {
+        if (it_pv < it_s) {
+          const int st = it_pv % L::NSTAGE;
+          if (p_ready(it_pv) && mbar_test(bar(L::B_VFULL + st), (it_pv / L::NSTAGE) & 1)) {
+            tc_fence_after();
+            // O_{t&1} += P(t) V(t): P from shared memory (K-major over keys), V MN-major (D contiguous)
+            const uint32_t pbase = sbase + L::OFF_P + (it_pv & 1) * L::PTILE;
+            const uint32_t vbase = sbase + L::OFF_V + st * L::TILE;
+            const uint32_t tO = tmem + 256 + (it_pv & 1) * 128;
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const uint64_t a = sw128_desc(pbase + (kk >> 2) * L::BOX + (kk & 3) * 32, 16, 1024);
+              const uint64_t bd = sw128_desc(vbase + kk * 16 * 128, L::BOX, 1024);
+              umma_ss(tO, a, bd, kIdescPV, (it_pv >= 2 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(bar(L::B_VEMPTY + st));
+            umma_commit(bar(L::B_PVDONE + (it_pv & 1)));
+            ++it_pv;
+            progress = true;
+          }
+        }
+        if (progress) {
+          t_prog = global_timer_ns();
+        } else if (*abort_flag) {
           ok = false;
-          break;
+        } else if (global_timer_ns() - t_prog > CEA_WAIT_LIMIT_NS) {
+          record_error(CEA_DEV_TIMEOUT_MMA);
+          *abort_flag = 1;
+          ok = false;
+        } else {
+          __nanosleep(20);  // leave issue slots to the softmax warps sharing this SMSP
         }
-        ++it;
       }
-      if (ok && it > 0) issue_pv(it - 1);
     }
-  }
   } else {
     // ================================================================ warpgroups 0, 1: softmax + epilogue
     asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
