@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(L::B_SFULL + s), 1);
-      mbar_init(bar(L::B_PFULL + s), 128);  // the warpgroup that owns tiles of parity s
+      mbar_init(bar(L::B_PFULL + s), 4);  // one arrival per warp of the warpgroup that owns parity s
       mbar_init(bar(L::B_PVDONE + s), 1);
     }
     *abort_flag = 0;
@@ -395,7 +395,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       fence_async_smem();  // P stores -> visible to the tensor-core (async) proxy
       tc_fence_before();
-      mbar_arrive(bar(L::B_PFULL + wg));
+      // one arrival per warp: 128 per-thread arrivals on one barrier are processed one by one and
+      // delayed the MMA issuer by about a thousand cycles per tile
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::B_PFULL + wg));
       ++it;
     }
 

@@ -1,34 +1,38 @@
-// Prefill attention with log-sum-exp, two query tiles per CTA (sm_100a, tcgen05).
+// Prefill attention with log-sum-exp, two query tiles per CTA sharing every K/V tile (sm_100a, tcgen05).
 //
 // A CTA owns two 128-row query tiles ("halves") that read the same KV head:
 // two query heads of one GQA group at the same positions, or two adjacent
-// query tiles of one head.  Every K/V tile is loaded once for both halves.
-//   warps 0-3 / 4-7   softmax of half 0 / half 1 (one thread per row = TMEM lane)
-//   warp 8            TMA producer (Q0, Q1, then a K ring and a V ring)
-//   warps 10-11       idle (they complete the third warpgroup for setmaxnreg)
-//   warp 9            MMA issuer, one thread:
-//                       S_h = Q_h K^T           (SS form, fp32 into TMEM)
-//                       O_h += P_h V            (TS form: P_h read from TMEM, V from smem)
-// TMEM (512 columns): half h owns columns [256h, 256h+128) for S_h -- P_h
-// (16-bit, two per column) is written over its first 64 columns once S_h has
-// been read -- and [256h+128, 256h+128+D) for O_h.
-//
-// The MMA thread issues, per half, PV_h(previous tile) then S_h(this tile).
-// tcgen05 operations of one thread complete in order, so when softmax h sees
-// S_h(t) complete, PV_h(t-1) has completed too: O_h may be rescaled and the
-// P_h columns rewritten without further waits.  The halves alternate, so one
-// half's softmax overlaps the other half's MMAs.
-//
-// Registers: the softmax warpgroups raise their budget to 232 with setmaxnreg
-// while the producer/MMA warpgroup drops to 40 (232 + 232 + 40 per SMSP stays
-// within the 168 x 3 the launch reserves), so a softmax thread holds its whole
-// S row in registers and reads TMEM with a single wait.
-//
-// Exponentials: ex2.approx on the MUFU pipe, except 3 of every 8 elements of
-// fully visible tiles, which use exp2_poly3 on the FMA pipe (round-to-nearest
-// range reduction, degree-3 least-squares fit of 2^f on [-0.5, 0.5], max
-// relative error 7.5e-5 -- far below the bf16 rounding applied to P).
+// query tiles of one head.  Each K/V tile is loaded once for both halves,
+// which halves the L2-to-SM traffic of the one-tile kernel.
+//   warps 0-3 / 4-7   softmax of half 0 / half 1: one thread per query row (=
+//                     TMEM lane) reads S_h into registers, masks, keeps the
+//                     running max/sum (log2 domain), writes P_h (16-bit pairs)
+//                     into the upper 64 columns of S_h, rescales O_h in TMEM when
+//                     its max grows by more than 2^8, and at the end normalises
+//                     O_h and writes out/lse (merging into the stored result in
+//                     accumulate mode)
+//   warp 8            TMA: Q0, Q1, then the K ring
+//   warp 10           TMA: the V ring
+//   warps 9 / 11      MMA issuer of half 0 / half 1, one thread each:
+//                       S_h(t) = Q_h K(t)^T      (SS form, fp32 into TMEM)
+//                       O_h += P_h(t) V(t)       (TS form: P_h read from TMEM)
+// Issuing a group of MMAs holds the issuing thread about as long as the group
+// runs.  The issuers take turns, each pushing the pair PV_h(t-1), S_h(t) after
+// the other half's previous pair: the tensor pipe then runs one half's pair
+// while the other half's softmax runs, the softmaxes of the two halves do not
+// compete, and each issuer's bookkeeping overlaps the other's MMAs.
+// Both halves process every key tile that either half can see (a tile one half
+// cannot see is processed as fully masked, P = 0), so both issuers release
+// every K and V stage and the stage barriers count one arrival per half.
+// TMEM (512 columns): half h owns [256h, 256h+128) for S_h / P_h and
+// [256h+128, 256h+128+D) for O_h.  P_h(t) overlays S_h(t), so S_h(t+1) is
+// issued only after PV_h(t).  tcgen05 operations of one thread execute in
+// issue order, which gives both guarantees the softmax relies on: S_h(t+1)
+// overwrites P_h(t) only after PV_h(t) has read it, and once S_h(t) is
+// complete PV_h(t-1) is complete too, so O_h may be rescaled in place.
 #pragma once
+
+#include <type_traits>
 
 #include "attn_tc.cuh"
 
@@ -37,10 +41,13 @@ namespace tc2 {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int NUM_THREADS = 384;  // three warpgroups: softmax 0, softmax 1, producer + MMA (+2 idle)
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int NUM_THREADS = 384;
+constexpr int kKProducerWarp = 8;  // Q tiles and the K ring
+constexpr int kMmaWarp = 9;         // MMA issuer of half 0; allocates TMEM
+constexpr int kVProducerWarp = 10;  // the V ring
+constexpr int kMmaWarp1 = 11;       // MMA issuer of half 1
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kPCol = 64;  // P_h columns within S_h (128 keys x 16 bit = 64 columns)
 constexpr float kRescaleThreshold = 8.0f;
 
 template <int D>
@@ -48,9 +55,9 @@ struct Layout {
   static constexpr int KBOX = D / 64;
   static constexpr int BOX = 128 * 128;
   static constexpr int TILE = KBOX * BOX;
-  static constexpr int KST = D == 128 ? 2 : 4;
-  static constexpr int VST = D == 128 ? 2 : 4;
-  static constexpr int OFF_Q = 0;  // two tiles
+  static constexpr int KST = D == 128 ? 3 : 5;  // K ring depth
+  static constexpr int VST = D == 128 ? 2 : 5;  // V ring depth
+  static constexpr int OFF_Q = 0;               // two tiles
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
   static constexpr int OFF_V = OFF_K + KST * TILE;
   static constexpr int OFF_BAR = OFF_V + VST * TILE;
@@ -62,7 +69,8 @@ struct Layout {
   static constexpr int B_SFULL = B_VEMPTY + VST;  // x2 (per half)
   static constexpr int B_PFULL = B_SFULL + 2;     // x2
   static constexpr int B_PVDONE = B_PFULL + 2;    // x2
-  static constexpr int NBAR = B_PVDONE + 2;
+  static constexpr int B_TURN = B_PVDONE + 2;     // x2: issuer h has pushed its next pair
+  static constexpr int NBAR = B_TURN + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = BYTES + 1024;
@@ -103,60 +111,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (*reinterpret_cast<volatile int*>(&g_cea_status) != 0) return;
 
   // ---------------------------------------------------------------- work of this CTA
+  // block -> (head pair or head, batch, query block), query blocks with the most keys first
+  // (scalars rather than 2-element arrays: a runtime index would put an array in local memory)
   int idx = blockIdx.x;
-  int head[2], qt[2];
-  bool active[2];
+  int head0, head1;
   if (pp.pair_heads) {
     const int hp = idx % (p.Hq / 2);
     idx /= (p.Hq / 2);
-    head[0] = 2 * hp;
-    head[1] = 2 * hp + 1;
-    const int b_ = idx % p.B;
-    (void)b_;
+    head0 = 2 * hp;
+    head1 = 2 * hp + 1;
   } else {
-    head[0] = head[1] = idx % p.Hq;
+    head0 = head1 = idx % p.Hq;
     idx /= p.Hq;
   }
   const int b = idx % p.B;
   idx /= p.B;
-  const int blk = pp.nblk_q - 1 - idx;  // most work first
-  if (pp.pair_heads) {
-    qt[0] = qt[1] = blk;
-  } else {
-    qt[0] = 2 * blk;
-    qt[1] = 2 * blk + 1;
-  }
-  active[0] = true;
-  active[1] = qt[1] < p.nqt;
-  const int kvh = p.kv_map ? p.kv_map[head[0]] : head[0] / p.group;
-  const TileStat qs0 = p.qstat[b * p.nqt + qt[0]];
-  const TileStat qs1 = active[1] ? p.qstat[b * p.nqt + qt[1]] : TileStat{LLONG_MAX, -1, 0, 0};
+  const int blk = pp.nblk_q - 1 - idx;
+  const int qt0 = pp.pair_heads ? blk : 2 * blk;
+  const int qt1 = pp.pair_heads ? blk : 2 * blk + 1;
+  const bool active1 = qt1 < p.nqt;  // an odd tile count leaves the last block with one half
+  const int kvh = p.kv_map ? p.kv_map[head0] : head0 / p.group;
+  const TileStat qs0 = p.qstat[b * p.nqt + qt0];
+  const TileStat qs1 = active1 ? p.qstat[b * p.nqt + qt1] : qs0;
   const TileStat* kst = p.kstat + static_cast<size_t>(b) * p.nkt;
   const bool causal = p.causal != 0;
-  int2 krange = p.qrange[b * p.nqt + qt[0]];
-  if (active[1]) {
-    const int2 r1 = p.qrange[b * p.nqt + qt[1]];
+  int2 krange = p.qrange[b * p.nqt + qt0];
+  if (active1) {
+    const int2 r1 = p.qrange[b * p.nqt + qt1];
     krange = make_int2(min(krange.x, r1.x), max(krange.y, r1.y));
   }
+  // class of key tile kt for half h (an inactive half skips everything)
   auto cls_of = [&](int h, int kt) -> int {
-    if (!active[h]) return kSkip;
+    if (h == 1 && !active1) return kSkip;
     return classify(h == 0 ? qs0 : qs1, kst[kt], causal);
   };
+  auto union_needed = [&](int kt) -> bool { return cls_of(0, kt) != kSkip || cls_of(1, kt) != kSkip; };
+  auto stat_needed = [&](const TileStat& ks) -> bool {
+    return classify(qs0, ks, causal) != kSkip || (active1 && classify(qs1, ks, causal) != kSkip);
+  };
+  const uint32_t n_halves = active1 ? 2u : 1u;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(L::B_QFULL), 1);
     for (int s = 0; s < L::KST; ++s) {
       mbar_init(bar(L::B_KFULL + s), 1);
-      mbar_init(bar(L::B_KEMPTY + s), 1);
+      mbar_init(bar(L::B_KEMPTY + s), n_halves);  // released by each half's S
     }
     for (int s = 0; s < L::VST; ++s) {
       mbar_init(bar(L::B_VFULL + s), 1);
-      mbar_init(bar(L::B_VEMPTY + s), 1);
+      mbar_init(bar(L::B_VEMPTY + s), n_halves);  // released by each half's PV
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(bar(L::B_SFULL + h), 1);
-      mbar_init(bar(L::B_PFULL + h), 128);
+      mbar_init(bar(L::B_PFULL + h), 4);  // one arrival per softmax warp
       mbar_init(bar(L::B_PVDONE + h), 1);
+      mbar_init(bar(L::B_TURN + h), 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -165,7 +174,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == kKProducerWarp && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
@@ -174,163 +183,172 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp >= 8) {
-  // ==================================================================== warpgroup 2
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
-  if (warp == kProducerWarp) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(bar(L::B_QFULL), (active[1] ? 2 : 1) * L::TILE);
-      for (int h = 0; h < 2; ++h) {
-        if (!active[h]) continue;
+
+  if (warp >= kKProducerWarp) {
+    // ================================================================ warpgroup 2
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
+    if ((warp == kKProducerWarp || warp == kVProducerWarp) && lane == 0) {
+      // ---------------------------------------------------------- TMA producers: Q + K ring, V ring
+      const bool is_k = warp == kKProducerWarp;
+      if (is_k) {
+        mbar_arrive_expect_tx(bar(L::B_QFULL), (active1 ? 2 : 1) * L::TILE);
 #pragma unroll
-        for (int kb = 0; kb < L::KBOX; ++kb)
-          tma_load_4d(sbase + L::OFF_Q + h * L::TILE + kb * L::BOX, &tmQ, bar(L::B_QFULL), kb * 64, qt[h] * BM,
-                      head[h], b);
+        for (int kb = 0; kb < L::KBOX; ++kb) {
+          tma_load_4d(sbase + L::OFF_Q + kb * L::BOX, &tmQ, bar(L::B_QFULL), kb * 64, qt0 * BM, head0, b);
+          if (active1)
+            tma_load_4d(sbase + L::OFF_Q + L::TILE + kb * L::BOX, &tmQ, bar(L::B_QFULL), kb * 64, qt1 * BM, head1, b);
+        }
       }
-      int u = 0;
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      const int nst = is_k ? L::KST : L::VST;
+      const int off = is_k ? L::OFF_K : L::OFF_V;
+      const int b_full = is_k ? L::B_KFULL : L::B_VFULL;
+      const int b_empty = is_k ? L::B_KEMPTY : L::B_VEMPTY;
+      int u = 0;  // union tile: a key tile at least one half needs
       for (int kt = krange.x; kt <= krange.y; ++kt) {
-        if (cls_of(0, kt) == kSkip && cls_of(1, kt) == kSkip) continue;
-        const int ks = u % L::KST, vs = u % L::VST;
-        const uint32_t kn = u / L::KST, vn = u / L::VST;
-        if (kn > 0 && !mbar_wait(bar(L::B_KEMPTY + ks), (kn - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(bar(L::B_KFULL + ks), L::TILE);
+        if (!union_needed(kt)) continue;
+        const int st = u % nst;
+        const uint32_t n = u / nst;
+        if (n > 0 && !mbar_wait(bar(b_empty + st), (n - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(bar(b_full + st), L::TILE);
 #pragma unroll
         for (int kb = 0; kb < L::KBOX; ++kb)
-          tma_load_4d(sbase + L::OFF_K + ks * L::TILE + kb * L::BOX, &tmK, bar(L::B_KFULL + ks), kb * 64, kt * BN,
-                      kvh, b);
-        if (vn > 0 && !mbar_wait(bar(L::B_VEMPTY + vs), (vn - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(bar(L::B_VFULL + vs), L::TILE);
-#pragma unroll
-        for (int kb = 0; kb < L::KBOX; ++kb)
-          tma_load_4d(sbase + L::OFF_V + vs * L::TILE + kb * L::BOX, &tmV, bar(L::B_VFULL + vs), kb * 64, kt * BN,
-                      kvh, b);
+          tma_load_4d(sbase + off + st * L::TILE + kb * L::BOX, map, bar(b_full + st), kb * 64, kt * BN, kvh, b);
         ++u;
       }
-    }
-  } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    } else if ((warp == kMmaWarp || (warp == kMmaWarp1 && active1)) && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer of half h (one thread)
+      // Pair j of half h is PV_h(j-1) (j >= 1) followed by S_h(j) (j < n); pairs j = 0..n.  Half 0 pushes
+      // pair j after half 1 has pushed pair j-1, half 1 pushes pair j after half 0 has pushed pair j, so
+      // turn_h completes once per pair and each wait below is one phase behind at most (unambiguous).
+      // The statistics of the next key tile are loaded a tile ahead, so advancing never waits for an L2
+      // round trip.
+      const int h = warp == kMmaWarp ? 0 : 1;
       constexpr uint32_t kIdescQK = idesc_f16(kBF16, false, BM, BN);
       constexpr uint32_t kIdescPV = idesc_f16(kBF16, true, BM, D);
+      const uint32_t tS = tmem + 256 * h;
+      const uint32_t tP = tS + kPCol;
+      const uint32_t tO = tS + 128;
+      const uint64_t qdesc = sw128_desc(sbase + L::OFF_Q + h * L::TILE, 16, 1024);
+      const uint64_t kdesc0 = sw128_desc(sbase + L::OFF_K, 16, 1024);
+      const uint64_t vdesc0 = sw128_desc(sbase + L::OFF_V, L::BOX, 1024);
       bool ok = mbar_wait(bar(L::B_QFULL), 0, abort_flag, CEA_DEV_TIMEOUT_MMA);
-      int it[2] = {0, 0};          // S issued per half
-      int pv[2] = {0, 0};          // PV issued per half
-      int prev_u[2] = {-1, -1};    // union index of the tile whose PV is pending, per half
-      int v_users[L::VST];         // halves still to read the V tile in each stage
-#pragma unroll
-      for (int s = 0; s < L::VST; ++s) v_users[s] = 0;
-      auto issue_pv = [&](int h) -> bool {
-        const int uu = prev_u[h];
-        const int vs = uu % L::VST;
-        if (!mbar_wait(bar(L::B_PFULL + h), (it[h] - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(bar(L::B_VFULL + vs), (uu / L::VST) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) return false;
-        tc_fence_after();
-        const uint32_t tP = tmem + 256 * h;
-        const uint32_t tO = tmem + 256 * h + 128;
-        const uint32_t vbase = sbase + L::OFF_V + vs * L::TILE;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_ts(tO, tP + kk * 8, sw128_desc(vbase + kk * 16 * 128, L::BOX, 1024), kIdescPV,
-                  (pv[h] > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(bar(L::B_PVDONE + h));
-        ++pv[h];
-        prev_u[h] = -1;
-        if (--v_users[vs] == 0) umma_commit(bar(L::B_VEMPTY + vs));
-        return true;
-      };
-      int u = 0;
-      for (int kt = krange.x; ok && kt <= krange.y; ++kt) {
-        const int c0 = cls_of(0, kt), c1 = cls_of(1, kt);
-        if (c0 == kSkip && c1 == kSkip) continue;
-        const int ks = u % L::KST;
-        if (!mbar_wait(bar(L::B_KFULL + ks), (u / L::KST) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) {
-          ok = false;
+      int kt = krange.x;
+      TileStat cur = kt <= krange.y ? kst[kt] : qs0;
+      while (kt <= krange.y && !stat_needed(cur)) {
+        ++kt;
+        if (kt <= krange.y) cur = kst[kt];
+      }
+      TileStat nxt = kt + 1 <= krange.y ? kst[kt + 1] : qs0;
+      for (int j = 0; ok; ++j) {
+        const bool has_s = kt <= krange.y;  // S_h(j) exists
+        // what this pair needs: K(j) for S_h(j), P_h(j-1) and V(j-1) for PV_h(j-1), the other half's turn
+        if (has_s && !mbar_wait(bar(L::B_KFULL + j % L::KST), (j / L::KST) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) break;
+        if (j > 0 && (!mbar_wait(bar(L::B_PFULL + h), (j - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA) ||
+                      !mbar_wait(bar(L::B_VFULL + (j - 1) % L::VST), ((j - 1) / L::VST) & 1, abort_flag,
+                                 CEA_DEV_TIMEOUT_MMA)))
           break;
+        if (active1) {
+          const bool turn_ok = h == 0 ? (j == 0 || mbar_wait(bar(L::B_TURN + 1), (j - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA))
+                                      : mbar_wait(bar(L::B_TURN + 0), j & 1, abort_flag, CEA_DEV_TIMEOUT_MMA);
+          if (!turn_ok) break;
         }
         tc_fence_after();
-        const uint32_t kbase = sbase + L::OFF_K + ks * L::TILE;
-        for (int h = 0; h < 2; ++h) {
-          // a pending PV is issued no later than the next union tile, even when this half skips
-          // it: the V stage it holds is what the producer needs next
-          if (prev_u[h] >= 0 && !issue_pv(h)) {
-            ok = false;
-            break;
-          }
-          if ((h == 0 ? c0 : c1) == kSkip) continue;
-          const uint32_t tS = tmem + 256 * h;
-          const uint32_t qbase = sbase + L::OFF_Q + h * L::TILE;
+        if (j > 0) {
+          const int vs = (j - 1) % L::VST;
+          const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * L::TILE) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            umma_ts(tO, tP + kk * 8, vdesc + static_cast<uint64_t>((kk * 16 * 128) >> 4), kIdescPV,
+                    (j > 1 || kk > 0) ? 1u : 0u);
+          umma_commit(bar(L::B_PVDONE + h));
+          umma_commit(bar(L::B_VEMPTY + vs));
+        }
+        if (has_s) {
+          const int ks = j % L::KST;
+          // descriptors differ from the tile's by the start address field only (addresses stay < 256 KB)
+          const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * L::TILE) >> 4);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
-            umma_ss(tS, sw128_desc(qbase + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), kIdescQK,
-                    kk > 0 ? 1u : 0u);
+            const uint32_t off = ((kk >> 2) * L::BOX + (kk & 3) * 32) >> 4;
+            umma_ss(tS, qdesc + off, kdesc + off, kIdescQK, kk > 0 ? 1u : 0u);
           }
           umma_commit(bar(L::B_SFULL + h));
-          ++it[h];
-          prev_u[h] = u;
-          ++v_users[u % L::VST];
+          umma_commit(bar(L::B_KEMPTY + ks));
         }
-        if (!ok) break;
-        umma_commit(bar(L::B_KEMPTY + ks));
-        ++u;
+        mbar_arrive(bar(L::B_TURN + h));
+        if (!has_s) break;  // that was the last pair
+        // next key tile any half can see, from the prefetched statistics
+        ++kt;
+        if (kt <= krange.y) {
+          cur = nxt;
+          while (kt <= krange.y && !stat_needed(cur)) {
+            ++kt;
+            if (kt <= krange.y) cur = kst[kt];
+          }
+          if (kt + 1 <= krange.y) nxt = kst[kt + 1];
+        }
       }
-      for (int h = 0; ok && h < 2; ++h)
-        if (prev_u[h] >= 0) ok = issue_pv(h);
     }
-  }
   } else {
-    // ==================================================================== warpgroups 0, 1: softmax + epilogue
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+    // ================================================================ warpgroups 0, 1: softmax + epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");
     const int h = warp >> 2;
+    const bool active = h == 0 || active1;
     const int row = threadIdx.x & 127;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + 256 * h + lane_base;
     const uint32_t tO = tmem + 256 * h + 128 + lane_base;
-    const int q_row = qt[h] * BM + row;
-    const bool row_in = active[h] && q_row < p.Sq;
+    const int q_row = (h == 0 ? qt0 : qt1) * BM + row;
+    const bool row_in = active && q_row < p.Sq;
     const long long qpos = row_in ? p.q_pos[b * p.qpos_sb + static_cast<int64_t>(q_row) * p.qpos_ss] : -1ll;
     const int64_t* kpos_b = p.k_pos + b * p.kpos_sb;
     float m = -INFINITY, l = 0.f;
-    int it = 0;
+    int it = 0;  // tiles processed by this half
     bool ok = true;
-    if (active[h]) {
+    if (active) {
       for (int kt = krange.x; kt <= krange.y; ++kt) {
-        const int cls = cls_of(h, kt);
-        if (cls == kSkip) continue;
+        const int cls_own = cls_of(h, kt);
+        const int cls_other = cls_of(h ^ 1, kt);
+        if (cls_own == kSkip && cls_other == kSkip) continue;
+        const int cls = cls_own == kSkip ? kMasked : cls_own;  // the other half's tile: every key masked here
         if (!tc::warp_wait(bar(L::B_SFULL + h), it & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // the whole S row in registers, one TMEM wait
-        uint32_t r[BN];
+        uint32_t s[BN];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-        uint32_t vis_bits[BN / 32];
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+        tmem_wait_ld();
+        float mx[8];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) vis_bits[c] = 0xffffffffu;
-        if (cls == kMasked) {  // overlaps the TMEM load
-#pragma unroll
+        for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
+        if (cls == kMasked) {
+          uint32_t vis[BN / 32];
+#pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t bits = 0u;
-            const int kbase = kt * BN + c * 32;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-              const int key = kbase + e;
+              const int key = kt * BN + c * 32 + e;
               const long long kp = key < p.Sk ? kpos_b[static_cast<int64_t>(key) * p.kpos_ss] : -1ll;
               bits |= (kp >= 0 && (!causal || kp <= qpos)) ? (1u << e) : 0u;
             }
-            vis_bits[c] = bits;
+            vis[c] = bits;
           }
-        }
-        tmem_wait_ld();
-        // the scale is positive, so it commutes with max
-        float rmax = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < BN; ++j)
-          rmax = fmaxf(rmax, ((vis_bits[j >> 5] >> (j & 31)) & 1u) ? __uint_as_float(r[j]) : -INFINITY);
-        const float tmax = rmax * p.scale_log2;
+          for (int j = 0; j < BN; ++j) {
+            if (!((vis[j >> 5] >> (j & 31)) & 1u)) s[j] = __float_as_uint(-INFINITY);
+            mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(s[j]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN; ++j) mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(s[j]));
+        }
+        const float tmax =
+            fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+            p.scale_log2;
         const float m_new = fmaxf(m, tmax);
         const bool rescale = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
         float alpha = 1.f;
@@ -341,8 +359,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           l *= alpha;
           m = m_new;
         }
-        const float m_use = (m == -INFINITY) ? 0.f : m;
-        // S_h(it) complete => PV_h(it-1) complete (in-order tcgen05): O_h is stable here
+        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+        // P_h = 2^(s*scale - m) as 16-bit pairs into the upper half of S_h (S is in registers)
+        float rs[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) rs[a] = 0.f;
+        auto emit = [&](auto use_poly) {
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float x0 = fmaf(__uint_as_float(s[c * 32 + 2 * e]), p.scale_log2, neg_m);
+              const float x1 = fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), p.scale_log2, neg_m);
+              const float p0 = (decltype(use_poly)::value && ((2 * e) & 7) >= 5) ? exp2_poly3(x0) : fast_exp2(x0);
+              const float p1 =
+                  (decltype(use_poly)::value && ((2 * e + 1) & 7) >= 5) ? exp2_poly3(x1) : fast_exp2(x1);
+              rs[(2 * e) & 7] += p0;
+              rs[(2 * e + 1) & 7] += p1;
+              pk[e] = pack2(p0, p1, kBF16);
+            }
+            tmem_st16(tS + kPCol + c * 16, pk);
+          }
+        };
+        if (CEA_POLY_EXP2 && cls == kFull) {
+          emit(std::true_type{});
+        } else {
+          emit(std::false_type{});
+        }
+        l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+        // S_h(it) complete => PV_h(it-1) complete: O_h is stable until P_h(it) is released
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
@@ -354,88 +400,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(tO + c * 32, o);
           }
         }
-        // P = 2^(s*scale - m) as 16-bit pairs over the first 64 S columns (already in registers)
-        float rowsum = 0.f;
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t pk[16];
-          const uint32_t bits = vis_bits[c];
-          if (cls == kFull) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float x0 = fmaf(__uint_as_float(r[c * 32 + 2 * e]), p.scale_log2, -m_use);
-              const float x1 = fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), p.scale_log2, -m_use);
-              // elements 5, 6, 7 of every 8 on the FMA pipe, the rest on MUFU
-              const float p0 = ((2 * e) & 7) >= 5 ? exp2_poly3(x0) : fast_exp2(x0);
-              const float p1 = ((2 * e + 1) & 7) >= 5 ? exp2_poly3(x1) : fast_exp2(x1);
-              rowsum += p0 + p1;
-              pk[e] = pack2(p0, p1, kBF16);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float x0 = ((bits >> (2 * e)) & 1u) ? fmaf(__uint_as_float(r[c * 32 + 2 * e]), p.scale_log2, -m_use)
-                                                        : -INFINITY;
-              const float x1 = ((bits >> (2 * e + 1)) & 1u)
-                                   ? fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), p.scale_log2, -m_use)
-                                   : -INFINITY;
-              const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-              rowsum += p0 + p1;
-              pk[e] = pack2(p0, p1, kBF16);
-            }
-          }
-          tmem_st16(tS + c * 16, pk);
-        }
-        l += rowsum;
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(L::B_PFULL + h));
+        // one arrival per warp: 128 per-thread arrivals on one barrier are processed one by one and
+        // delayed the MMA issuer by about a thousand cycles per tile
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::B_PFULL + h));
         ++it;
       }
     }
 
     // ---------------------------------------------------------------- epilogue
+    // PV_h(it-1) is the last product in O_h.  S_h(it-1) completed, hence PV_h(it-2) did: pv_done_h has
+    // completed it-1 or it phases, so the parity wait is unambiguous.
     if (ok && it > 0) {
       ok = tc::warp_wait(bar(L::B_PVDONE + h), (it - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
       tc_fence_after();
     }
-    if (ok && active[h] && !(it == 0 && p.accumulate)) {
-      const int hh = head[h];
+    if (ok && active && !(it == 0 && p.accumulate)) {
+      const int hh = h == 0 ? head0 : head1;
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const float lse_row = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
       float w_old = 0.f, w_new = 1.f, lse_out = lse_row;
       float* lse_ptr = p.lse ? p.lse + b * p.l_sb + hh * p.l_sh + static_cast<int64_t>(q_row) * p.l_ss : nullptr;
       if (p.accumulate && row_in) {
         const float lse_old = *lse_ptr;
-        const float mx = fmaxf(lse_old, lse_row);
-        if (mx == -INFINITY) {
+        const float mxl = fmaxf(lse_old, lse_row);
+        if (mxl == -INFINITY) {
           lse_out = -INFINITY;
           w_new = 0.f;
         } else {
-          lse_out = mx + log1pf(expf(-fabsf(lse_old - lse_row)));
+          lse_out = mxl + log1pf(expf(-fabsf(lse_old - lse_row)));
           w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - lse_out);
           w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - lse_out);
         }
       }
-      const float scale_new = inv_l * w_new;
+      const float c_new = inv_l * w_new;
       const int64_t obase = b * p.o_sb + static_cast<int64_t>(q_row) * p.o_ss + hh * p.o_sh;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t o[16];
         if (it > 0) {
-          tmem_ld32(tO + c * 32, o);
+          tmem_ld16(tO + c * 16, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0u;
+          for (int e = 0; e < 16; ++e) o[e] = 0u;
         }
         if (!row_in) continue;
         if (p.out_dtype == CEA_F32) {
-          float* dst = reinterpret_cast<float*>(p.out) + obase + c * 32;
+          float* dst = reinterpret_cast<float*>(p.out) + obase + c * 16;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float4 v = make_float4(__uint_as_float(o[e]) * scale_new, __uint_as_float(o[e + 1]) * scale_new,
-                                   __uint_as_float(o[e + 2]) * scale_new, __uint_as_float(o[e + 3]) * scale_new);
+          for (int e = 0; e < 16; e += 4) {
+            float4 v = make_float4(__uint_as_float(o[e]) * c_new, __uint_as_float(o[e + 1]) * c_new,
+                                   __uint_as_float(o[e + 2]) * c_new, __uint_as_float(o[e + 3]) * c_new);
             if (p.accumulate) {
               const float4 old = *reinterpret_cast<const float4*>(dst + e);
               v.x += old.x * w_old;
@@ -446,14 +464,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             *reinterpret_cast<float4*>(dst + e) = v;
           }
         } else {
-          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + obase + c * 32;
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + obase + c * 16;
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
+          for (int e = 0; e < 16; e += 8) {
             uint4 v;
-            v.x = pack2(__uint_as_float(o[e]) * scale_new, __uint_as_float(o[e + 1]) * scale_new, kBF16);
-            v.y = pack2(__uint_as_float(o[e + 2]) * scale_new, __uint_as_float(o[e + 3]) * scale_new, kBF16);
-            v.z = pack2(__uint_as_float(o[e + 4]) * scale_new, __uint_as_float(o[e + 5]) * scale_new, kBF16);
-            v.w = pack2(__uint_as_float(o[e + 6]) * scale_new, __uint_as_float(o[e + 7]) * scale_new, kBF16);
+            v.x = pack2(__uint_as_float(o[e]) * c_new, __uint_as_float(o[e + 1]) * c_new, kBF16);
+            v.y = pack2(__uint_as_float(o[e + 2]) * c_new, __uint_as_float(o[e + 3]) * c_new, kBF16);
+            v.z = pack2(__uint_as_float(o[e + 4]) * c_new, __uint_as_float(o[e + 5]) * c_new, kBF16);
+            v.w = pack2(__uint_as_float(o[e + 6]) * c_new, __uint_as_float(o[e + 7]) * c_new, kBF16);
             *reinterpret_cast<uint4*>(dst + e) = v;
           }
         }

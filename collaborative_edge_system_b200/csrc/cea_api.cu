@@ -223,11 +223,13 @@ int launch_empty(const cea_attn_params* p, cudaStream_t s) {
   return cuda_check("fill_empty_kernel");
 }
 
-// which prefill kernel generation runs (CEA_PREFILL_KERNEL=2 selects the two-tile kernel under evaluation)
+// Which tcgen05 prefill kernel runs: 2 (default) = two query tiles per CTA sharing each K/V tile
+// (attn_tc2.cuh); CEA_PREFILL_KERNEL=1 selects the one-tile kernel (attn_tc.cuh), kept as a
+// reference point for measurements and as a fallback.
 int prefill_version() {
   static int v = [] {
     const char* e = getenv("CEA_PREFILL_KERNEL");
-    return (e != nullptr && e[0] == '2') ? 2 : 1;
+    return (e != nullptr && e[0] == '1') ? 1 : 2;
   }();
   return v;
 }
