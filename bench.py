@@ -51,6 +51,11 @@ def _peaks():
         return 1590.0, 1400.0, 6650.0, "fallback"
 
 
+def prefill_kernel_name() -> str:
+    """The tcgen05 prefill kernel libcea.so runs (CEA_PREFILL_KERNEL=1 selects the one-tile kernel)."""
+    return "attn_fwd_tc_kernel" if os.environ.get("CEA_PREFILL_KERNEL", "") == "1" else "attn_fwd_tc2_kernel"
+
+
 def _traffic_summary():
     """Per-launch DRAM bytes of the dominant kernels from a committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -198,8 +203,9 @@ def bench_prefill(cea, rank, world, dev, steps, warmup):
     kern_ms = sum(s.elapsed_time(e) for s, e in ev[launches_before:])
     kern_ms_per_step = kern_ms / steps
     n_attn = (len(ev) - launches_before) // steps  # attention calls per step
-    # our kernels per attention call: two tile-stat passes + the tcgen05 kernel
-    gpu_launches = steps * n_attn * 3
+    # our kernels per attention call: query and key tile statistics, the per-query-tile key range,
+    # then the tcgen05 kernel
+    gpu_launches = steps * n_attn * 4
     return {
         "ms_per_step": ms / steps,
         "tflops": total_flops * steps / (ms / 1e3) / 1e12,
@@ -359,8 +365,8 @@ def ncu_case(which: str, warmup: int) -> None:
     """A few launches of one kernel on a case sized for an ncu capture.
 
     prefill: causal GQA attention, 16384 tokens (q 128 MiB + k/v 32 MiB each: inputs beyond L2),
-    1/16 of the benchmark's queries x 1/8 of its keys on average -> one launch of attn_fwd_tc_kernel
-    per call.  decode: the benchmark's decode shape with a 16384-token cache (512 MiB of K+V).
+    1/16 of the benchmark's queries x 1/8 of its keys on average -> one launch of the tcgen05 prefill
+    kernel per call.  decode: the benchmark's decode shape with a 16384-token cache (512 MiB of K+V).
     """
     import collaborative_edge_system_b200 as cea
 
@@ -454,9 +460,9 @@ def main():
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1), q scaled by 1/sqrt(128))",
         "config": config,
-        "roofline": {"bound": "tensor", "kernel": "attn_fwd_tc_kernel", "achieved": kt, "peak": peak_burst,
+        "roofline": {"bound": "tensor", "kernel": prefill_kernel_name(), "achieved": kt, "peak": peak_burst,
                      "unit": "TFLOP/s", "frac": kt / peak_burst, "frac_of_sustained": kt / peak_sus,
-                     "peak_source": peak_kind, "traffic": traffic.get("attn_fwd_tc_kernel_bytes_per_launch"),
+                     "peak_source": peak_kind, "traffic": traffic.get(prefill_kernel_name() + "_bytes_per_launch"),
                      "flops_per_launch": pre["flops_rank"] / max(1, pre["launches_per_step"]),
                      "kernel_ms_per_step": pre["kernel_ms_per_step"]},
         "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},

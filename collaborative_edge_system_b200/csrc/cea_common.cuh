@@ -92,33 +92,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
-// Same contract as mbar_wait, but polls with test_wait instead of sleeping in try_wait: for a
-// thread on the critical path of a pipeline (an MMA issuer), where waking from try_wait has been
-// measured to cost several hundred cycles.  The clock and the abort flag are read every 1024 polls.
-__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
-  uint32_t n = 0;
-  uint64_t t0 = 0;
-  while (!mbar_test(bar, parity)) {
-    if ((++n & 1023u) == 0) {
-      if (abort != nullptr && *abort) return false;
-      if (n == 1024) {
-        t0 = global_timer_ns();
-      } else if (global_timer_ns() - t0 > CEA_WAIT_LIMIT_NS) {
-        record_error(code);
-        if (abort != nullptr) *abort = 1;
-        return false;
-      }
-    }
-  }
-  return true;
-}
-
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 // 4-D tiled load into this CTA's shared memory; completion is signalled on `bar`
-// through the transaction count (no cluster multicast: every CTA loads its own tiles).
+// through the transaction count.  Every CTA loads its own tiles from this GPU's memory.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
                                             int c2, int c3) {
   asm volatile(
