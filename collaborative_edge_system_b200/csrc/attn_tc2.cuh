@@ -111,9 +111,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (*reinterpret_cast<volatile int*>(&g_cea_status) != 0) return;
 
   // ---------------------------------------------------------------- work of this CTA
-  // block -> (head pair or head, batch, query block), query blocks with the most keys first
+  // block -> (query block, head pair or head, batch), query blocks fastest and those with the most keys
+  // first: the CTAs in flight then read the K/V of one or two KV heads, which stay in L2, instead of
+  // streaming every KV head of the sequence through it at once
   // (scalars rather than 2-element arrays: a runtime index would put an array in local memory)
   int idx = blockIdx.x;
+  const int blk = pp.nblk_q - 1 - idx % pp.nblk_q;
+  idx /= pp.nblk_q;
   int head0, head1;
   if (pp.pair_heads) {
     const int hp = idx % (p.Hq / 2);
@@ -124,9 +128,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     head0 = head1 = idx % p.Hq;
     idx /= p.Hq;
   }
-  const int b = idx % p.B;
-  idx /= p.B;
-  const int blk = pp.nblk_q - 1 - idx;
+  const int b = idx;
   const int qt0 = pp.pair_heads ? blk : 2 * blk;
   const int qt1 = pp.pair_heads ? blk : 2 * blk + 1;
   const bool active1 = qt1 < p.nqt;  // an odd tile count leaves the last block with one half
