@@ -462,7 +462,9 @@ def main():
         "config": config,
         "roofline": {"bound": "tensor", "kernel": prefill_kernel_name(), "achieved": kt, "peak": peak_burst,
                      "unit": "TFLOP/s", "frac": kt / peak_burst, "frac_of_sustained": kt / peak_sus,
-                     "peak_source": peak_kind, "traffic": traffic.get(prefill_kernel_name() + "_bytes_per_launch"),
+                     "peak_source": peak_kind,
+                     # measured on the 1-GPU launch only; a rank's launch at N > 1 covers a different slice
+                     "traffic": traffic.get(prefill_kernel_name() + "_bytes_per_launch") if world == 1 else None,
                      "flops_per_launch": pre["flops_rank"] / max(1, pre["launches_per_step"]),
                      "kernel_ms_per_step": pre["kernel_ms_per_step"]},
         "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},
