@@ -38,6 +38,7 @@ if ROOT not in sys.path:
 
 S_TOTAL, HQ, HKV, D = 131072, 32, 8, 128
 DEC_B, DEC_T, DEC_STEPS, DEC_WARM = 16, 131072, 256, 8
+UL_B, UL_S, UL_H = 2, 65536, 32  # Ulysses side metric: MHA, uneven shards at 4 ranks
 METRIC = "causal SP prefill attention TFLOP/s at 1/2/4/8 B200; split-KV decode tok/s"
 
 
@@ -252,6 +253,44 @@ def bench_prefill_e2e(cea, rank, world, dev, steps, warmup, layout, tensors, com
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / steps}
 
 
+# ----------------------------------------------------------------------------- ours: Ulysses
+def bench_ulysses(cea, rank, world, dev, steps, warmup):
+    """Causal Ulysses prefill (all-to-all sequence <-> heads), MHA B=2, 32 heads, D=128, 65536 tokens.
+
+    At 4 ranks the shards are uneven as the engine builds them for weights 0.4/0.3/0.2/0.1: tokens
+    split_sizes(65536, w, granularity=128) = [26112, 19584, 13184, 6656] and heads partition_heads(32, 32, w)
+    = [12, 9, 7, 4]; otherwise the split is even.
+    """
+    weights = [0.4, 0.3, 0.2, 0.1] if world == 4 else world
+    seq = cea.split_sizes(UL_S, weights, granularity=128)
+    heads = cea.partition_heads(UL_H, UL_H, weights)
+    off, s_loc = sum(seq[:rank]), seq[rank]
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    q, k, v = (torch.randn(UL_B, s_loc, UL_H, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    pos = torch.arange(off, off + s_loc, device=dev).repeat(UL_B, 1)
+    comm = cea.ParallelContext(1, world, 1, device=dev).sp
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        return cea.ulysses_attention(q, k, v, pos, comm, seq, heads, causal=True, scale=scale)[0]
+
+    for _ in range(warmup):
+        step()
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world, dev)
+    flops = 4.0 * UL_B * UL_H * D * (UL_S * (UL_S + 1) / 2)
+    return {"metric": "Ulysses causal prefill TFLOP/s", "value": flops * steps / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ms / steps, "steps": steps,
+            "config": {"batch": UL_B, "seq_len": UL_S, "q_heads": UL_H, "kv_heads": UL_H, "head_dim": D,
+                       "seq_sizes": seq, "heads_per_rank": [hs.q_count for hs in heads]}}
+
+
 # ----------------------------------------------------------------------------- ours: decode
 def bench_decode(cea, rank, world, dev):
     from collaborative_edge_system_b200 import _lib
@@ -401,6 +440,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-ulysses", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--ncu-case", choices=["prefill", "decode"], default=None,
                     help="run a small case of one kernel for an ncu capture (no timing, no JSON line)")
@@ -442,6 +482,7 @@ def main():
                             pre["tensors"], pre["comm"])
     del pre["tensors"]
     dec = None if args.no_decode else bench_decode(cea, rank, world, dev)
+    uly = None if args.no_ulysses else bench_ulysses(cea, rank, world, dev, args.steps, warmup)
     status = _lib.device_status(clear=True)
     peak_burst, peak_sus, hbm, peak_kind = _peaks()
     traffic = _traffic_summary()
@@ -481,6 +522,8 @@ def main():
                                        "peak": hbm, "unit": "GB/s", "frac": dec["hbm_frac"],
                                        "traffic": traffic.get("decode_partial_kernel_bytes_per_launch"),
                                        "kernel_ms": dec["kernel_ms"]}}
+    if uly is not None:
+        line["ulysses"] = uly
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:

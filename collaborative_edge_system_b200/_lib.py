@@ -19,7 +19,9 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libcea.so")
 F32, F16, BF16, F64 = 0, 1, 2, 3
 _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
 
-CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE = range(6)
+CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE, CEA_ERR_NCCL = range(7)
+ABI_VERSION = 2
+NCCL_ID_BYTES = 128
 MAX_MERGE = 32
 MAX_SEGMENTS = 64
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -116,6 +118,13 @@ EXPORTS = (
     "cea_device_status",
     "cea_last_error",
     "cea_abi_version",
+    "cea_nccl_get_unique_id",
+    "cea_nccl_comm_init",
+    "cea_nccl_comm_destroy",
+    "cea_nccl_abort",
+    "cea_ring_step",
+    "cea_alltoallv",
+    "cea_allgather",
 )
 
 _lib: Optional[ctypes.CDLL] = None
@@ -147,11 +156,19 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             ("cea_device_status", [ctypes.POINTER(ctypes.c_int), ctypes.c_int, P], ctypes.c_int),
             ("cea_last_error", [], ctypes.c_char_p),
             ("cea_abi_version", [], ctypes.c_int),
+            ("cea_nccl_get_unique_id", [P], ctypes.c_int),
+            ("cea_nccl_comm_init", [ctypes.POINTER(P), ctypes.c_int, ctypes.c_int, P], ctypes.c_int),
+            ("cea_nccl_comm_destroy", [P], ctypes.c_int),
+            ("cea_nccl_abort", [P], ctypes.c_int),
+            ("cea_ring_step", [P, P, ctypes.c_size_t, ctypes.c_int, P, ctypes.c_size_t, ctypes.c_int, P], ctypes.c_int),
+            ("cea_alltoallv", [P, P, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t), P,
+                               ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t), P], ctypes.c_int),
+            ("cea_allgather", [P, P, P, ctypes.c_size_t, P], ctypes.c_int),
         ):
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        if lib.cea_abi_version() != 1:
+        if lib.cea_abi_version() != ABI_VERSION:
             raise RuntimeError("libcea.so ABI version mismatch; rebuild it")
         _lib = lib
         return lib

@@ -46,7 +46,7 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     if not force and up_to_date():
         return LIB
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-I", INCLUDE, "-o", tmp, os.path.join(CSRC, "cea_api.cu"), "-lcudart"]
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-I", INCLUDE, "-o", tmp, os.path.join(CSRC, "cea_api.cu"), "-lcudart", "-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -8,11 +8,13 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "attn_simt.cuh"
 #include "attn_tc.cuh"
 #include "attn_tc2.cuh"
 #include "cea_common.cuh"
+#include "cea_nccl.cuh"
 #include "decode.cuh"
 
 using namespace cea;
@@ -693,6 +695,140 @@ int cea_device_status(int* status_out, int clear, void* stream) {
     if (cudaMemcpyToSymbol(g_cea_status, &zero, sizeof(int)) != cudaSuccess) return cuda_check("cea_device_status");
   }
   if (status_out) *status_out = v;
+  return CEA_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------- NCCL
+namespace {
+
+int nccl_fail(const char* what, cea::nccl::Result r) {
+  const auto& a = cea::nccl::api();
+  return fail(CEA_ERR_NCCL, "%s: %s", what, a.error_string ? a.error_string(r) : "NCCL error");
+}
+
+int nccl_ready() {
+  const auto& a = cea::nccl::api();
+  return a.ok ? CEA_OK : fail(CEA_ERR_NCCL, "%s", a.why.c_str());
+}
+
+bool rank_ok(const cea_nccl_comm* c, int r) { return r >= 0 && r < c->nranks; }
+
+}  // namespace
+
+extern "C" {
+
+int cea_nccl_get_unique_id(void* id_out) {
+  if (id_out == nullptr) return fail(CEA_ERR_INVALID, "cea_nccl_get_unique_id: null id buffer");
+  if (int e = nccl_ready()) return e;
+  cea::nccl::UniqueId id;
+  if (const auto r = cea::nccl::api().get_unique_id(&id)) return nccl_fail("ncclGetUniqueId", r);
+  memcpy(id_out, id.internal, CEA_NCCL_ID_BYTES);
+  return CEA_OK;
+}
+
+int cea_nccl_comm_init(cea_nccl_comm** comm_out, int rank, int nranks, const void* id) {
+  if (comm_out == nullptr || id == nullptr) return fail(CEA_ERR_INVALID, "cea_nccl_comm_init: null argument");
+  *comm_out = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(CEA_ERR_INVALID, "cea_nccl_comm_init: rank %d out of range for %d ranks", rank, nranks);
+  if (int e = nccl_ready()) return e;
+  cea::nccl::UniqueId uid;
+  memcpy(uid.internal, id, CEA_NCCL_ID_BYTES);
+  cea::nccl::Comm nc = nullptr;
+  if (const auto r = cea::nccl::api().comm_init_rank(&nc, nranks, uid, rank)) return nccl_fail("ncclCommInitRank", r);
+  *comm_out = new cea_nccl_comm{nc, rank, nranks};
+  return CEA_OK;
+}
+
+int cea_nccl_comm_destroy(cea_nccl_comm* comm) {
+  if (comm == nullptr) return CEA_OK;
+  const auto r = cea::nccl::api().comm_destroy(comm->comm);
+  delete comm;
+  return r ? nccl_fail("ncclCommDestroy", r) : CEA_OK;
+}
+
+int cea_nccl_abort(cea_nccl_comm* comm) {
+  if (comm == nullptr) return CEA_OK;
+  const auto r = cea::nccl::api().comm_abort(comm->comm);
+  delete comm;
+  return r ? nccl_fail("ncclCommAbort", r) : CEA_OK;
+}
+
+int cea_ring_step(cea_nccl_comm* comm, const void* send, size_t send_bytes, int to, void* recv, size_t recv_bytes,
+                  int from, void* stream) {
+  if (comm == nullptr) return fail(CEA_ERR_INVALID, "cea_ring_step: null communicator");
+  if (!rank_ok(comm, to) || !rank_ok(comm, from))
+    return fail(CEA_ERR_INVALID, "cea_ring_step: peer out of range (to %d, from %d, %d ranks)", to, from, comm->nranks);
+  if ((send_bytes > 0 && send == nullptr) || (recv_bytes > 0 && recv == nullptr))
+    return fail(CEA_ERR_INVALID, "cea_ring_step: null buffer");
+  const auto s = static_cast<cudaStream_t>(stream);
+  if (to == comm->rank || from == comm->rank) {  // a ring of one: the block stays local
+    if (to != from || send_bytes != recv_bytes)
+      return fail(CEA_ERR_INVALID, "cea_ring_step: a self transfer needs to == from and equal sizes");
+    if (send_bytes > 0 && cudaMemcpyAsync(recv, send, send_bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return cuda_check("cea_ring_step");
+    return CEA_OK;
+  }
+  const auto& a = cea::nccl::api();
+  if (int e = nccl_ready()) return e;
+  if (const auto r = a.group_start()) return nccl_fail("ncclGroupStart", r);
+  cea::nccl::Result r = 0;
+  if (send_bytes > 0) r = a.send(send, send_bytes, cea::nccl::kUint8, to, comm->comm, s);
+  if (r == 0 && recv_bytes > 0) r = a.recv(recv, recv_bytes, cea::nccl::kUint8, from, comm->comm, s);
+  const auto r2 = a.group_end();
+  if (r) return nccl_fail("ncclSend/ncclRecv", r);
+  return r2 ? nccl_fail("ncclGroupEnd", r2) : CEA_OK;
+}
+
+int cea_alltoallv(cea_nccl_comm* comm, const void* send, const size_t* send_bytes, const size_t* send_offsets,
+                  void* recv, const size_t* recv_bytes, const size_t* recv_offsets, void* stream) {
+  if (comm == nullptr || send_bytes == nullptr || send_offsets == nullptr || recv_bytes == nullptr ||
+      recv_offsets == nullptr)
+    return fail(CEA_ERR_INVALID, "cea_alltoallv: null argument");
+  const int n = comm->nranks, me = comm->rank;
+  for (int p = 0; p < n; ++p)
+    if ((send_bytes[p] > 0 && send == nullptr) || (recv_bytes[p] > 0 && recv == nullptr))
+      return fail(CEA_ERR_INVALID, "cea_alltoallv: null buffer");
+  if (send_bytes[me] != recv_bytes[me])
+    return fail(CEA_ERR_INVALID, "cea_alltoallv: this rank sends itself %zu bytes but expects %zu", send_bytes[me],
+                recv_bytes[me]);
+  const auto s = static_cast<cudaStream_t>(stream);
+  const auto* sb = static_cast<const uint8_t*>(send);
+  auto* rb = static_cast<uint8_t*>(recv);
+  if (send_bytes[me] > 0 &&
+      cudaMemcpyAsync(rb + recv_offsets[me], sb + send_offsets[me], send_bytes[me], cudaMemcpyDeviceToDevice, s) !=
+          cudaSuccess)
+    return cuda_check("cea_alltoallv");
+  if (n == 1) return CEA_OK;
+  const auto& a = cea::nccl::api();
+  if (int e = nccl_ready()) return e;
+  if (const auto r = a.group_start()) return nccl_fail("ncclGroupStart", r);
+  cea::nccl::Result r = 0;
+  for (int p = 0; p < n && r == 0; ++p) {
+    if (p == me) continue;
+    if (send_bytes[p] > 0) r = a.send(sb + send_offsets[p], send_bytes[p], cea::nccl::kUint8, p, comm->comm, s);
+    if (r == 0 && recv_bytes[p] > 0) r = a.recv(rb + recv_offsets[p], recv_bytes[p], cea::nccl::kUint8, p, comm->comm, s);
+  }
+  const auto r2 = a.group_end();
+  if (r) return nccl_fail("ncclSend/ncclRecv", r);
+  return r2 ? nccl_fail("ncclGroupEnd", r2) : CEA_OK;
+}
+
+int cea_allgather(cea_nccl_comm* comm, const void* send, void* recv, size_t bytes, void* stream) {
+  if (comm == nullptr) return fail(CEA_ERR_INVALID, "cea_allgather: null communicator");
+  if (bytes > 0 && (send == nullptr || recv == nullptr)) return fail(CEA_ERR_INVALID, "cea_allgather: null buffer");
+  if (bytes == 0) return CEA_OK;
+  const auto s = static_cast<cudaStream_t>(stream);
+  if (comm->nranks == 1) {
+    if (recv != send && cudaMemcpyAsync(recv, send, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return cuda_check("cea_allgather");
+    return CEA_OK;
+  }
+  if (int e = nccl_ready()) return e;
+  if (const auto r = cea::nccl::api().all_gather(send, recv, bytes, cea::nccl::kUint8, comm->comm, s))
+    return nccl_fail("ncclAllGather", r);
   return CEA_OK;
 }
 

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define CEA_ABI_VERSION 1
+#define CEA_ABI_VERSION 2
 
 enum cea_status {
   CEA_OK = 0,
@@ -34,7 +34,8 @@ enum cea_status {
   CEA_ERR_UNSUPPORTED = 2, /* dtype / shape combination without a kernel */
   CEA_ERR_CUDA = 3,        /* CUDA runtime or driver error */
   CEA_ERR_WORKSPACE = 4,   /* workspace missing or too small */
-  CEA_ERR_DEVICE = 5       /* a kernel reported a device-side error (see cea_device_status) */
+  CEA_ERR_DEVICE = 5,      /* a kernel reported a device-side error (see cea_device_status) */
+  CEA_ERR_NCCL = 6         /* NCCL library missing, or an NCCL call failed */
 };
 
 /* device-side error codes stored by kernels (bounded waits that expired) */
@@ -180,6 +181,47 @@ typedef struct cea_copy_params {
 
 int cea_ulysses_pack(const cea_copy_params* p, void* stream);
 int cea_ulysses_unpack(const cea_copy_params* p, void* stream);
+
+/*
+ * NCCL transfers of the sequence-parallel path, for callers that hold no
+ * PyTorch process group.  They stand in for collab_infer's Communicator
+ * (distributed/comm.py:200) and its set-up:
+ *   cea_nccl_get_unique_id / cea_nccl_comm_init  - process-group creation
+ *     (init_distributed, distributed/launcher.py:55-97; the per-axis
+ *     Communicators of distributed/mesh.py:89-110);
+ *   cea_nccl_comm_destroy / cea_nccl_abort       - teardown;
+ *   cea_ring_step  - the grouped send to r+1 / receive from r-1 of one ring
+ *     attention step (parallel/sequence_parallel.py:108-116 over
+ *     Communicator.isend/irecv, comm.py:574-610);
+ *   cea_alltoallv  - the uneven all-to-all of ulysses_scatter/gather
+ *     (sequence_parallel.py:163-194, Communicator.all_to_all, comm.py:468-524);
+ *   cea_allgather  - the all-gather of distributed_kv_attention and
+ *     gather_sequence (sequence_parallel.py:50-62,270-276,
+ *     Communicator.all_gather_list, comm.py:369-410).
+ * NCCL is loaded at run time: CEA_NCCL_LIBRARY if set, else the libnccl.so.2
+ * already loaded in the process, else libnccl.so.2 from the loader path.
+ * Buffers are device memory of the communicator's GPU, sizes in bytes; the
+ * transfers are enqueued on `stream` and never synchronise the host.
+ * cea_nccl_comm_init binds the communicator to the current CUDA device and,
+ * like every NCCL initialisation, blocks until all ranks have called it.
+ */
+#define CEA_NCCL_ID_BYTES 128
+typedef struct cea_nccl_comm cea_nccl_comm;
+
+/* A fresh NCCL unique id (CEA_NCCL_ID_BYTES bytes) for rank 0 to hand to the others. */
+int cea_nccl_get_unique_id(void* id_out);
+int cea_nccl_comm_init(cea_nccl_comm** comm_out, int rank, int nranks, const void* id);
+int cea_nccl_comm_destroy(cea_nccl_comm* comm);
+/* Aborts outstanding NCCL work of the communicator and frees it (error paths). */
+int cea_nccl_abort(cea_nccl_comm* comm);
+/* Sends send_bytes to rank `to` and receives recv_bytes from rank `from`, as one NCCL group. */
+int cea_ring_step(cea_nccl_comm* comm, const void* send, size_t send_bytes, int to, void* recv, size_t recv_bytes,
+                  int from, void* stream);
+/* Uneven all-to-all: nranks-entry arrays of byte counts and byte offsets into send / recv. */
+int cea_alltoallv(cea_nccl_comm* comm, const void* send, const size_t* send_bytes, const size_t* send_offsets,
+                  void* recv, const size_t* recv_bytes, const size_t* recv_offsets, void* stream);
+/* recv (nranks * bytes) receives every rank's `bytes` bytes in rank order. */
+int cea_allgather(cea_nccl_comm* comm, const void* send, void* recv, size_t bytes, void* stream);
 
 /* Reads (and with clear != 0 resets) the device error word of the current device. Synchronises `stream`. */
 int cea_device_status(int* status_out, int clear, void* stream);

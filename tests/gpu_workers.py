@@ -74,3 +74,59 @@ def decode_worker(rank, world, T, B, Hq, Hkv, D):
     out = cea.distributed_kv_attention(q.to(dev), kl, vl, qp.to(dev), pl, ctx.sp)
     ref = oracle.attention(_np(q), _np(k), _np(v), qp.numpy(), kp.numpy(), True)
     return float(np.abs(_np(out) - ref).max()), str(out.dtype)
+
+
+def nccl_abi_worker(rank, world):
+    """libcea.so's own NCCL communicator: ring step, uneven all-to-all and all-gather between the GPUs."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    from collaborative_edge_system_b200 import _lib
+
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    idt = torch.zeros(_lib.NCCL_ID_BYTES, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        raw = ctypes.create_string_buffer(_lib.NCCL_ID_BYTES)
+        assert lib.cea_nccl_get_unique_id(raw) == 0, lib.cea_last_error()
+        idt.copy_(torch.frombuffer(bytearray(raw.raw), dtype=torch.uint8))
+    dist.broadcast(idt, 0)  # rank 0 hands the id out over the test's own process group
+    idbuf = ctypes.create_string_buffer(bytes(idt.cpu().tolist()), _lib.NCCL_ID_BYTES)
+    comm = ctypes.c_void_p()
+    assert lib.cea_nccl_comm_init(ctypes.byref(comm), rank, world, idbuf) == 0, lib.cea_last_error()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    res = {}
+
+    # ring step: r sends to r+1 and receives from r-1, uneven sizes
+    nxt, prv = (rank + 1) % world, (rank - 1) % world
+    send = torch.arange(1000 + 10 * rank, device=dev, dtype=torch.int32) + 100000 * rank
+    recv = torch.full((1000 + 10 * prv,), -1, device=dev, dtype=torch.int32)
+    rc = lib.cea_ring_step(comm, send.data_ptr(), send.numel() * 4, nxt, recv.data_ptr(), recv.numel() * 4, prv, stream)
+    assert rc == 0, lib.cea_last_error()
+    torch.cuda.synchronize(dev)
+    res["ring"] = torch.equal(recv, torch.arange(1000 + 10 * prv, device=dev, dtype=torch.int32) + 100000 * prv)
+
+    # uneven all-to-all: rank r sends (r + 1) * (p + 3) int32 values to rank p, valued 1000 r + p
+    cnt = lambda r, p: (r + 1) * (p + 3)  # noqa: E731
+    sb = [cnt(rank, p) * 4 for p in range(world)]
+    rb = [cnt(p, rank) * 4 for p in range(world)]
+    so = [sum(sb[:p]) for p in range(world)]
+    ro = [sum(rb[:p]) for p in range(world)]
+    src = torch.cat([torch.full((cnt(rank, p),), 1000 * rank + p, dtype=torch.int32, device=dev) for p in range(world)])
+    dst = torch.full((sum(rb) // 4,), -1, dtype=torch.int32, device=dev)
+    arr = lambda xs: (ctypes.c_size_t * world)(*xs)  # noqa: E731
+    rc = lib.cea_alltoallv(comm, src.data_ptr(), arr(sb), arr(so), dst.data_ptr(), arr(rb), arr(ro), stream)
+    assert rc == 0, lib.cea_last_error()
+    torch.cuda.synchronize(dev)
+    want = torch.cat([torch.full((cnt(p, rank),), 1000 * p + rank, dtype=torch.int32, device=dev) for p in range(world)])
+    res["alltoallv"] = torch.equal(dst, want)
+
+    # all-gather of 333 bytes per rank
+    part = torch.full((333,), rank + 7, dtype=torch.uint8, device=dev)
+    full = torch.zeros(333 * world, dtype=torch.uint8, device=dev)
+    assert lib.cea_allgather(comm, part.data_ptr(), full.data_ptr(), 333, stream) == 0, lib.cea_last_error()
+    torch.cuda.synchronize(dev)
+    res["allgather"] = torch.equal(full, torch.arange(world, device=dev).repeat_interleave(333).to(torch.uint8) + 7)
+    assert lib.cea_nccl_comm_destroy(comm) == 0, lib.cea_last_error()
+    return res

@@ -29,7 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.cea_abi_version() == 1
+    assert lib.cea_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
@@ -45,6 +45,23 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     c = _lib.CopyParams()
     c.n, c.D, c.elem_bytes = 1, 8, 3
     assert lib.cea_ulysses_pack(ctypes.byref(c), None) == _lib.CEA_ERR_INVALID
+
+
+def test_nccl_entry_points_reject_bad_arguments_without_nccl_or_gpu():
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    assert lib.cea_nccl_get_unique_id(None) == _lib.CEA_ERR_INVALID
+    comm = P()
+    idbuf = ctypes.create_string_buffer(_lib.NCCL_ID_BYTES)
+    assert lib.cea_nccl_comm_init(ctypes.byref(comm), 2, 2, idbuf) == _lib.CEA_ERR_INVALID  # rank 2 of 2
+    assert b"out of range" in lib.cea_last_error()
+    assert comm.value is None
+    assert lib.cea_ring_step(None, None, 0, 1, None, 0, 1, None) == _lib.CEA_ERR_INVALID
+    sizes = (ctypes.c_size_t * 2)(0, 0)
+    assert lib.cea_alltoallv(None, None, sizes, sizes, None, sizes, sizes, None) == _lib.CEA_ERR_INVALID
+    assert lib.cea_allgather(None, None, None, 16, None) == _lib.CEA_ERR_INVALID
+    assert lib.cea_nccl_comm_destroy(None) == _lib.CEA_OK
+    assert lib.cea_nccl_abort(None) == _lib.CEA_OK
 
 
 def test_product_path_refuses_cpu_tensors():

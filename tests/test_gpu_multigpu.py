@@ -39,3 +39,9 @@ def test_distributed_kv_decode_nccl():
     for eo, dtype in _run(W.decode_worker, 2, 3000, 4, 8, 2, 128):
         assert eo < 2e-2
         assert dtype == "torch.bfloat16"
+
+
+def test_libcea_nccl_entry_points():
+    """The C ABI's own NCCL communicator (for callers without a torch process group) moves the same bytes."""
+    for res in _run(W.nccl_abi_worker, 2):
+        assert res == {"ring": True, "alltoallv": True, "allgather": True}, res
