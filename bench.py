@@ -11,7 +11,9 @@ B=16, 32/8 heads, 131072-token bf16 cache sharded over the ranks, 256 steps
 each appending one token to the last rank's shard - tokens/s and HBM GB/s.
 
 ``e2e`` repeats the prefill through the public API with inputs copied from
-pinned host memory and the output copied back inside the timed region.
+pinned host memory and the output copied back inside the timed region, every
+step, double-buffered so that the next step's input copies overlap the current
+step's compute.
 ``--impl reference`` times the reference algorithm's CPU restatement
 (``oracle/``, numpy + OpenBLAS, all host threads) on a bounded sample of the
 same workload; rank 0 alone runs it.
@@ -224,33 +226,63 @@ def bench_prefill(cea, rank, world, dev, steps, warmup):
 
 
 def bench_prefill_e2e(cea, rank, world, dev, steps, warmup, layout, tensors, comm):
-    """Same step through the public API, inputs from pinned host memory, output back to the host."""
+    """Same step through the public API with host buffers: every step copies its inputs from pinned host memory
+    and its output back, as a serving loop would, double-buffered so that step i+1's inputs travel on a copy
+    stream while step i computes (each step's copies stay inside the timed region)."""
     q, k, v, pos = tensors
-    hq, hk, hv, hp = (t.cpu().pin_memory() for t in (q, k, v, pos))
-    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    hosts = tuple(t.cpu().pin_memory() for t in (q, k, v, pos))
+    hout = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2)]
+    dbuf = [tuple(torch.empty_like(t, device=dev) for t in hosts) for _ in range(2)]
     scale = 1.0 / math.sqrt(D)
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hp))
-    d2h = hout.numel() * hout.element_size()
+    h2d = sum(t.numel() * t.element_size() for t in hosts)
+    d2h = hout[0].numel() * hout[0].element_size()
+    main = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    loaded = [torch.cuda.Event() for _ in range(2)]  # inputs of buffer j are on the device
+    consumed = [torch.cuda.Event() for _ in range(2)]  # the step reading buffer j has finished
+    for e in consumed:
+        e.record(main)
 
-    def step():
-        dq, dk, dv, dp = (t.to(dev, non_blocking=True) for t in (hq, hk, hv, hp))
+    def load(i):
+        j = i % 2
+        with torch.cuda.stream(copy):
+            copy.wait_event(consumed[j])
+            for d, h in zip(dbuf[j], hosts):
+                d.copy_(h, non_blocking=True)
+            loaded[j].record(copy)
+
+    def compute(i):
+        j = i % 2
+        main.wait_event(loaded[j])
+        dq, dk, dv, dp = dbuf[j]
         out = cea.ring_attention(dq, dk, dv, dp, dp, comm, layout.sizes, causal=True, scale=scale)
-        hout.copy_(out, non_blocking=True)
+        consumed[j].record(main)
+        with torch.cuda.stream(copy):
+            copy.wait_event(consumed[j])
+            out.record_stream(copy)
+            hout[j].copy_(out, non_blocking=True)
 
-    for _ in range(max(1, warmup // 2)):
-        step()
+    def run(n):
+        load(0)
+        for i in range(n):
+            if i + 1 < n:
+                load(i + 1)
+            compute(i)
+        main.wait_stream(copy)
+
+    run(max(1, warmup // 2))
     barrier(world)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        step()
-    t1.record()
+    t0.record(main)
+    run(steps)
+    t1.record(main)
     barrier(world)
     ms = max_over_ranks(t0.elapsed_time(t1), world, dev)
     total_flops = 4.0 * HQ * D * (S_TOTAL * (S_TOTAL + 1) / 2)
     return {"value": total_flops * steps / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": ms / steps}
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms / steps, "steps": steps,
+            "overlap": "double-buffered: step i+1's host-to-device copies run during step i"}
 
 
 # ----------------------------------------------------------------------------- ours: Ulysses
@@ -478,8 +510,7 @@ def main():
     rank, world, dev = setup(args.gpus)
     warmup = max(3, args.warmup)
     pre = bench_prefill(cea, rank, world, dev, args.steps, warmup)
-    e2e = bench_prefill_e2e(cea, rank, world, dev, max(1, min(args.steps, 3)), warmup, pre["layout"],
-                            pre["tensors"], pre["comm"])
+    e2e = bench_prefill_e2e(cea, rank, world, dev, args.steps, warmup, pre["layout"], pre["tensors"], pre["comm"])
     del pre["tensors"]
     dec = None if args.no_decode else bench_decode(cea, rank, world, dev)
     uly = None if args.no_ulysses else bench_ulysses(cea, rank, world, dev, args.steps, warmup)
@@ -508,7 +539,7 @@ def main():
                      "traffic": traffic.get(prefill_kernel_name() + "_bytes_per_launch") if world == 1 else None,
                      "flops_per_launch": pre["flops_rank"] / max(1, pre["launches_per_step"]),
                      "kernel_ms_per_step": pre["kernel_ms_per_step"]},
-        "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+        "e2e": {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step", "steps", "overlap")},
         "gpu_launches": pre["gpu_launches"],
         "clocks": {k: pre["clocks"][k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
         "device_status": status,
