@@ -70,7 +70,11 @@ def _traffic_summary():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms while running.
+
+    Started before the warm-up so that it is already sampling when the timed region begins (``wait_first``);
+    the summary is the median over the samples taken while the GPU was running the benchmark's steps.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -81,24 +85,43 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        import threading
+
+        self.lines = []
+        self._first = threading.Event()
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            self._first.set()
+            return self
+
+        def reader():
+            for line in self.proc.stdout:
+                if line.strip():
+                    self.lines.append(line)
+                    self._first.set()
+            self._first.set()
+
+        self._thread = threading.Thread(target=reader, daemon=True)
+        self._thread.start()
         return self
 
+    def wait_first(self, timeout: float = 5.0) -> None:
+        """Block until nvidia-smi has produced its first sample (or gave up)."""
+        self._first.wait(timeout)
+
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+                self.proc.wait()
+            self._thread.join(timeout=5)
         return False
 
     def summary(self):
@@ -187,12 +210,13 @@ def bench_prefill(cea, rank, world, dev, steps, warmup):
     def step():
         return cea.ring_attention(q, k, v, pos, pos, comm, layout.sizes, causal=True, scale=scale)
 
-    for _ in range(warmup):
-        step()
-    barrier(world)
-    attn_mod.attend_into = sp_mod.attend_into = timed_attend
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
+        for _ in range(warmup):
+            step()
+        clk.wait_first()
+        barrier(world)
+        attn_mod.attend_into = sp_mod.attend_into = timed_attend
         barrier(world)
         start.record()
         for _ in range(steps):
