@@ -284,6 +284,32 @@ def merge(outs: Sequence[torch.Tensor], lses: Sequence[torch.Tensor], out: torch
     _check(load().cea_merge(ctypes.byref(p), _stream_ptr(out.device)), "cea_merge")
 
 
+def merge_stacked(parts: torch.Tensor, D: int, out: torch.Tensor) -> None:
+    """cea_merge over n <= MAX_MERGE partials stacked as ``parts[n, B, Sq, H, W]`` (fp32 or fp64, W > D): each
+    partial's output in columns ``[0, D)`` and its lse in column ``D``.  The pointers and strides come from
+    the stacked tensor directly, so no per-partial views are built."""
+    n, B, Sq, H, W = parts.shape
+    if W <= D or parts.stride(4) != 1:
+        raise ValueError("stacked partials need rows of more than D contiguous elements")
+    st = parts.stride()
+    es = parts.element_size()
+    base = parts.data_ptr()
+    p = MergeParams()
+    p.n = n
+    for i in range(n):
+        p.outs[i] = base + i * st[0] * es
+        p.lses[i] = base + (i * st[0] + D) * es
+    p.out = out.data_ptr()
+    p.lse = None
+    p.part_o_stride = _i64x3(st[1], st[2], st[3])    # b, s, h
+    p.part_lse_stride = _i64x3(st[1], st[3], st[2])  # b, h, s
+    p.o_stride = _i64x3(out.stride(0), out.stride(1), out.stride(2))
+    p.B, p.Sq, p.H, p.D = B, Sq, H, D
+    p.part_dtype = dtype_code(parts.dtype)
+    p.out_dtype = dtype_code(out.dtype)
+    _check(load().cea_merge(ctypes.byref(p), _stream_ptr(out.device)), "cea_merge")
+
+
 def copy_segments(segments, D: int, elem_bytes: int, device: torch.device, entry: str = "cea_ulysses_pack") -> None:
     """Run cea_ulysses_pack / unpack over ``(src, dst, nb, ns, nh)`` tensor segments.
 

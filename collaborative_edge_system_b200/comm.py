@@ -368,6 +368,22 @@ class Communicator:
                     lambda: dist.all_gather(outs, buf, group=self.group))
         return [self._to(o.narrow(dim, 0, s), t.device) for o, s in zip(outs, sizes)]
 
+    def all_gather_stacked(self, t: torch.Tensor) -> torch.Tensor:
+        """Equal-shaped ``t`` from every rank as one ``[size, *t.shape]`` tensor, rank-major.
+
+        On NCCL this is a single ``all_gather_into_tensor`` with no per-rank views, for callers that hand the
+        result to a kernel as one buffer (the decode merge).  Accounted like :meth:`all_gather_list`.
+        """
+        if self.size == 1:
+            return t.unsqueeze(0)
+        if self.on_device and self.small_message_bytes == 0:
+            buf = self._to_comm(t.contiguous())
+            flat = torch.empty((self.size,) + tuple(buf.shape), dtype=buf.dtype, device=buf.device)
+            self._timed("all_gather", _nbytes(buf) * (self.size - 1), self.size - 1,
+                        lambda: dist.all_gather_into_tensor(flat, buf, group=self.group))
+            return flat
+        return torch.stack(self.all_gather_list(t, dim=0))
+
     def all_gather(self, t: torch.Tensor, dim: int = 0, sizes: Optional[Sequence[int]] = None,
                    compress: bool = False) -> torch.Tensor:
         if self.size == 1:

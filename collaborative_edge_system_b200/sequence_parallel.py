@@ -260,20 +260,33 @@ def distributed_kv_attention(
 ) -> torch.Tensor:
     """Replicated queries against a sequence-sharded cache (``sequence_parallel.py:250-280``).
 
-    Each rank attends over its shard (split-KV decode kernel); one all-gather
-    of ``[B, Sq, H, D+1]`` partials and an exact n-way merge follow.
+    Each rank attends over its shard (split-KV decode kernel), writing its
+    partial straight into a packed ``[B, Sq, H, D+4]`` message (out, lse,
+    padding); one all-gather of the messages and an exact n-way merge over
+    the gathered buffer follow.
     """
-    o, l = attention_with_lse(q, k_local, v_local, q_pos, k_pos_local, causal=causal, scale=scale, kv_map=kv_map,
-                              kv_block=kv_block)
     if comm.size == 1:
+        o, _ = attention_with_lse(q, k_local, v_local, q_pos, k_pos_local, causal=causal, scale=scale,
+                                  kv_map=kv_map, kv_block=kv_block)
         return o.to(q.dtype)
-    D = o.shape[-1]
-    packed = torch.cat([o, l.transpose(1, 2).unsqueeze(-1)], dim=-1)
-    parts = comm.all_gather_list(packed, dim=0)
+    # the local partial goes straight into the packed [B, Sq, H, D+4] message: out in [0, D), lse at D, rows
+    # padded to 16 bytes so the kernels keep their vector stores
+    B, Sq, Hq, D = q.shape
+    packed = torch.empty(B, Sq, Hq, D + 4, dtype=accumulation_dtype(q.dtype), device=q.device)
+    attend_into(q, k_local, v_local, q_pos, k_pos_local, packed[..., :D], packed[..., D].permute(0, 2, 1),
+                causal=causal, scale=scale, kv_map=kv_map)
+    return _merge_stacked(comm.all_gather_stacked(packed), D, q.dtype)
+
+
+def _merge_stacked(parts: torch.Tensor, D: int, out_dtype: torch.dtype) -> torch.Tensor:
+    """Exact merge of the partials stacked as ``parts[n, B, Sq, H, W]`` (out in [0, D), lse at D)."""
+    if parts.is_cuda and parts.shape[0] <= _lib.MAX_MERGE:
+        out = torch.empty(parts.shape[1:-1] + (D,), dtype=out_dtype, device=parts.device)
+        _lib.merge_stacked(parts, D, out)
+        return out
     outs: List[torch.Tensor] = [p[..., :D] for p in parts]
     lses: List[torch.Tensor] = [p[..., D].transpose(1, 2) for p in parts]
-    out, _ = _merge(outs, lses, out_dtype=q.dtype)
-    return out
+    return _merge(outs, lses, out_dtype=out_dtype)[0]
 
 
 __all__ = [
