@@ -271,3 +271,24 @@ def test_merge_kernel_vs_oracle():
     m, ml = cea.merge_attention_list([o.to(DEV) for o in outs], [l.to(DEV) for l in lses])
     _cmp(_np(m), ref_o, 1e-5)
     _cmp(_np(ml), ref_l, 1e-5)
+
+
+@pytest.mark.parametrize("n", [3, 8, 40])
+def test_stacked_merge_equals_view_merge(n):
+    # the distributed-KV decode merges partials gathered as one [n, B, Sq, H, D+4] buffer (out, lse, padding);
+    # the result must equal the merge over per-partial views bit for bit, also past 32 partials (fallback path)
+    from collaborative_edge_system_b200.sequence_parallel import _merge_stacked
+
+    B, Sq, H, D = 2, 3, 5, 128
+    g = torch.Generator(device=DEV).manual_seed(n)
+    parts = torch.randn(n, B, Sq, H, D + 4, generator=g, device=DEV)
+    parts[..., D] = torch.randn(n, B, Sq, H, generator=g, device=DEV) * 4
+    parts[0, 0, 0, 0, D] = float("-inf")  # an empty partial for one row
+    outs = [p[..., :D] for p in parts]
+    lses = [p[..., D].transpose(1, 2) for p in parts]
+    ref = cea.merge_attention_list(outs, lses)[0].to(torch.bfloat16)
+    got = _merge_stacked(parts, D, torch.bfloat16)
+    assert got.dtype == torch.bfloat16 and got.shape == (B, Sq, H, D)
+    assert torch.equal(got, ref)
+    ref32 = cea.merge_attention_list(outs, lses)[0]
+    assert torch.equal(_merge_stacked(parts, D, torch.float32), ref32)
