@@ -22,6 +22,8 @@ _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, tor
 CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE, CEA_ERR_NCCL = range(7)
 ABI_VERSION = 2
 NCCL_ID_BYTES = 128
+MAX_PEERS = 16
+IPC_HANDLE_BYTES = 64
 MAX_MERGE = 32
 MAX_SEGMENTS = 64
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -85,6 +87,24 @@ class MergeParams(ctypes.Structure):
     ]
 
 
+class PeerMergeParams(ctypes.Structure):
+    _fields_ = [
+        ("n", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("bufs", ctypes.c_void_p * MAX_PEERS),
+        ("flags", ctypes.c_void_p * MAX_PEERS),
+        ("epoch", ctypes.c_uint64),
+        ("B", ctypes.c_int32),
+        ("Sq", ctypes.c_int32),
+        ("H", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("W", ctypes.c_int32),
+        ("out", ctypes.c_void_p),
+        ("o_stride", _i64x3),
+        ("out_dtype", ctypes.c_int32),
+    ]
+
+
 class Segment(ctypes.Structure):
     _fields_ = [
         ("src", ctypes.c_void_p),
@@ -125,6 +145,10 @@ EXPORTS = (
     "cea_ring_step",
     "cea_alltoallv",
     "cea_allgather",
+    "cea_peer_merge",
+    "cea_ipc_export",
+    "cea_ipc_open",
+    "cea_ipc_close",
 )
 
 _lib: Optional[ctypes.CDLL] = None
@@ -164,6 +188,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             ("cea_alltoallv", [P, P, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t), P,
                                ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t), P], ctypes.c_int),
             ("cea_allgather", [P, P, P, ctypes.c_size_t, P], ctypes.c_int),
+            ("cea_peer_merge", [ctypes.POINTER(PeerMergeParams), P], ctypes.c_int),
+            ("cea_ipc_export", [P, P, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+            ("cea_ipc_open", [P, ctypes.c_size_t, ctypes.POINTER(P), ctypes.POINTER(P)], ctypes.c_int),
+            ("cea_ipc_close", [P], ctypes.c_int),
         ):
             fn = getattr(lib, name)
             fn.argtypes = args
@@ -308,6 +336,40 @@ def merge_stacked(parts: torch.Tensor, D: int, out: torch.Tensor) -> None:
     p.part_dtype = dtype_code(parts.dtype)
     p.out_dtype = dtype_code(out.dtype)
     _check(load().cea_merge(ctypes.byref(p), _stream_ptr(out.device)), "cea_merge")
+
+
+def ipc_export(t: torch.Tensor):
+    """(handle bytes, offset) of the device allocation holding ``t``, for another process of this node."""
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = ctypes.c_size_t()
+    _check(load().cea_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "cea_ipc_export")
+    return h.raw, off.value
+
+
+def ipc_open(handle: bytes, offset: int):
+    """Maps a peer's exported allocation on the current device: (pointer, base to pass to ipc_close)."""
+    h = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+    _check(load().cea_ipc_open(h, offset, ctypes.byref(ptr), ctypes.byref(base)), "cea_ipc_open")
+    return ptr.value, base.value
+
+
+def ipc_close(base: int) -> None:
+    _check(load().cea_ipc_close(base), "cea_ipc_close")
+
+
+def peer_merge(n: int, rank: int, bufs, flags, epoch: int, W: int, out: torch.Tensor) -> None:
+    """cea_peer_merge: push this rank's slot to every peer, wait for theirs, merge into ``out [B, Sq, H, D]``."""
+    p = PeerMergeParams()
+    p.n, p.rank, p.epoch, p.W = n, rank, epoch, W
+    for q in range(n):
+        p.bufs[q] = bufs[q]
+        p.flags[q] = flags[q]
+    p.B, p.Sq, p.H, p.D = out.shape
+    p.out = out.data_ptr()
+    p.o_stride = _i64x3(out.stride(0), out.stride(1), out.stride(2))
+    p.out_dtype = dtype_code(out.dtype)
+    _check(load().cea_peer_merge(ctypes.byref(p), _stream_ptr(out.device)), "cea_peer_merge")
 
 
 def copy_segments(segments, D: int, elem_bytes: int, device: torch.device, entry: str = "cea_ulysses_pack") -> None:

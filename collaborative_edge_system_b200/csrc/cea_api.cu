@@ -16,6 +16,7 @@
 #include "cea_common.cuh"
 #include "cea_nccl.cuh"
 #include "decode.cuh"
+#include "peer_merge.cuh"
 
 using namespace cea;
 
@@ -830,6 +831,101 @@ int cea_allgather(cea_nccl_comm* comm, const void* send, void* recv, size_t byte
   if (const auto r = cea::nccl::api().all_gather(send, recv, bytes, cea::nccl::kUint8, comm->comm, s))
     return nccl_fail("ncclAllGather", r);
   return CEA_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------ peer-memory decode merge
+extern "C" {
+
+int cea_peer_merge(const cea_peer_merge_params* p, void* stream) {
+  if (p == nullptr || p->n < 1 || p->n > CEA_MAX_PEERS || p->rank < 0 || p->rank >= p->n)
+    return fail(CEA_ERR_INVALID, "cea_peer_merge: need 1..%d ranks and a rank among them", CEA_MAX_PEERS);
+  if (p->epoch < 1) return fail(CEA_ERR_INVALID, "cea_peer_merge: calls are numbered from 1");
+  if (p->B < 0 || p->Sq < 0 || p->H < 0 || p->D < 1 || p->W <= p->D || p->W % 4 != 0)
+    return fail(CEA_ERR_INVALID, "cea_peer_merge: invalid sizes (W must be a multiple of 4 greater than D)");
+  if (p->out == nullptr) return fail(CEA_ERR_INVALID, "cea_peer_merge: null output");
+  if (p->out_dtype != CEA_F32 && p->out_dtype != CEA_BF16 && p->out_dtype != CEA_F16)
+    return fail(CEA_ERR_UNSUPPORTED, "cea_peer_merge: output dtype must be F32, BF16 or F16");
+  for (int q = 0; q < p->n; ++q)
+    if (p->bufs[q] == nullptr || p->flags[q] == nullptr || !aligned16(p->bufs[q]) ||
+        (reinterpret_cast<uintptr_t>(p->flags[q]) & 7u) != 0)
+      return fail(CEA_ERR_INVALID, "cea_peer_merge: rank %d's buffer or counters missing or misaligned", q);
+  const int64_t rows = static_cast<int64_t>(p->B) * p->Sq * p->H;
+  if (rows == 0) return CEA_OK;
+  peer::Args a;
+  a.n = p->n;
+  a.rank = p->rank;
+  a.par = static_cast<int>(p->epoch & 1u);
+  for (int q = 0; q < CEA_MAX_PEERS; ++q) {
+    a.bufs[q] = q < p->n ? p->bufs[q] : nullptr;
+    a.flags[q] = q < p->n ? reinterpret_cast<unsigned long long*>(p->flags[q]) : nullptr;
+  }
+  a.target = static_cast<unsigned long long>(peer::kGrid) * p->epoch;
+  a.rows = rows;
+  a.W = p->W;
+  a.D = p->D;
+  a.B = p->B;
+  a.Sq = p->Sq;
+  a.H = p->H;
+  a.out = p->out;
+  a.o_sb = p->o_stride[0];
+  a.o_ss = p->o_stride[1];
+  a.o_sh = p->o_stride[2];
+  const auto s = static_cast<cudaStream_t>(stream);
+  if (p->out_dtype == CEA_F32) {
+    peer::peer_merge_kernel<float><<<peer::kGrid, peer::kThreads, 0, s>>>(a);
+  } else if (p->out_dtype == CEA_BF16) {
+    peer::peer_merge_kernel<__nv_bfloat16><<<peer::kGrid, peer::kThreads, 0, s>>>(a);
+  } else {
+    peer::peer_merge_kernel<__half><<<peer::kGrid, peer::kThreads, 0, s>>>(a);
+  }
+  return cuda_check("peer_merge_kernel");
+}
+
+int cea_ipc_export(const void* ptr, void* handle_out, size_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return fail(CEA_ERR_INVALID, "cea_ipc_export: null argument");
+  typedef CUresult (*RangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range = nullptr;
+  if (range == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(CEA_ERR_CUDA, "cea_ipc_export: cuMemGetAddressRange unavailable");
+    range = reinterpret_cast<RangeFn>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(CEA_ERR_INVALID, "cea_ipc_export: %p is not device memory", ptr);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(CEA_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  static_assert(sizeof(h) == CEA_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return CEA_OK;
+}
+
+int cea_ipc_open(const void* handle, size_t offset, void** ptr_out, void** base_out) {
+  if (handle == nullptr || ptr_out == nullptr || base_out == nullptr)
+    return fail(CEA_ERR_INVALID, "cea_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(CEA_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  *base_out = base;
+  *ptr_out = static_cast<uint8_t*>(base) + offset;
+  return CEA_OK;
+}
+
+int cea_ipc_close(void* base) {
+  if (base == nullptr) return CEA_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  return e == cudaSuccess ? CEA_OK : fail(CEA_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
 }
 
 }  // extern "C"

@@ -22,9 +22,11 @@ is where the work runs:
 
 from __future__ import annotations
 
+import os
 from typing import List, Optional, Sequence, Tuple
 
 import torch
+import torch.distributed as dist
 
 from . import _lib
 from .attention import KVMap, accumulation_dtype, attend_into, attention, attention_with_lse, _merge
@@ -272,10 +274,88 @@ def distributed_kv_attention(
     # the local partial goes straight into the packed [B, Sq, H, D+4] message: out in [0, D), lse at D, rows
     # padded to 16 bytes so the kernels keep their vector stores
     B, Sq, Hq, D = q.shape
+    W = D + 4
+    pd = _peer_decode(comm, B * Sq * Hq * W, q)
+    if pd is not None:
+        # one node, peers mapped: the partial goes into this rank's slot of its own receive buffer, and one
+        # kernel pushes it to every peer, waits for theirs and merges (no NCCL call)
+        pd.epoch += 1
+        slot = pd.slot(pd.epoch & 1, comm.rank).view(B, Sq, Hq, W)
+        attend_into(q, k_local, v_local, q_pos, k_pos_local, slot[..., :D], slot[..., D].permute(0, 2, 1),
+                    causal=causal, scale=scale, kv_map=kv_map)
+        out = torch.empty(B, Sq, Hq, D, dtype=q.dtype, device=q.device)
+        _lib.peer_merge(comm.size, comm.rank, pd.bufs, pd.flags, pd.epoch, W, out)
+        comm.stats.record(f"{comm.name}.all_gather", slot.numel() * 4 * (comm.size - 1), 0.0)
+        return out
     packed = torch.empty(B, Sq, Hq, D + 4, dtype=accumulation_dtype(q.dtype), device=q.device)
     attend_into(q, k_local, v_local, q_pos, k_pos_local, packed[..., :D], packed[..., D].permute(0, 2, 1),
                 causal=causal, scale=scale, kv_map=kv_map)
     return _merge_stacked(comm.all_gather_stacked(packed), D, q.dtype)
+
+
+class _PeerDecode:
+    """Receive slots and counters of the peer-memory decode merge for one communicator.
+
+    One device allocation per rank holds 2 parities x n ranks x ``slot_floats`` floats followed by n uint64
+    counters (zeroed); every rank maps every peer's allocation (CUDA IPC).  Built collectively on the first
+    multi-rank decode call: if any rank cannot map its peers (no peer access, ranks on several nodes), all
+    ranks agree to keep the all-gather path.
+    """
+
+    def __init__(self, comm: Communicator, slot_floats: int, device: torch.device):
+        n, r = comm.size, comm.rank
+        self.slot_floats, self.epoch, self.bases = slot_floats, 0, []
+        data = 2 * n * slot_floats
+        self.mem = torch.zeros(data + 2 * n, dtype=torch.float32, device=device)  # counters after the slots
+        torch.cuda.synchronize(device)  # zeroed before any peer can add to the counters
+        try:
+            mine = _lib.ipc_export(self.mem)
+        except RuntimeError:
+            mine = None
+        infos = [None] * n
+        dist.all_gather_object(infos, mine, group=comm.group)
+        self.bufs, self.flags = [0] * n, [0] * n
+        ok = all(i is not None for i in infos)
+        for q in range(n):
+            if not ok:
+                break
+            if q == r:
+                ptr = self.mem.data_ptr()
+            else:
+                try:
+                    ptr, base = _lib.ipc_open(*infos[q])
+                except RuntimeError:
+                    ok = False
+                    break
+                self.bases.append(base)
+            self.bufs[q], self.flags[q] = ptr, ptr + data * 4
+        oks = [None] * n
+        dist.all_gather_object(oks, ok, group=comm.group)  # also: every rank has mapped before any push
+        self.ok = all(oks)
+        if not self.ok:
+            self.close()
+
+    def slot(self, par: int, rank: int) -> torch.Tensor:
+        n = len(self.bufs)
+        return self.mem[: 2 * n * self.slot_floats].view(2, n, self.slot_floats)[par, rank]
+
+    def close(self) -> None:
+        for base in self.bases:
+            _lib.ipc_close(base)
+        self.bases = []
+
+
+def _peer_decode(comm: Communicator, slot_floats: int, q: torch.Tensor) -> Optional[_PeerDecode]:
+    """The communicator's peer-memory decode exchange, if it applies to this call (the same decision on every
+    rank: it depends only on the communicator, the environment and the shapes)."""
+    if (os.environ.get("CEA_PEER_DECODE", "1") == "0" or not comm.on_device or comm.size > _lib.MAX_PEERS
+            or not q.is_cuda or accumulation_dtype(q.dtype) != torch.float32):
+        return None
+    pd = getattr(comm, "_cea_peer_decode", None)
+    if pd is None:
+        pd = _PeerDecode(comm, slot_floats, q.device)
+        comm._cea_peer_decode = pd
+    return pd if pd.ok and pd.slot_floats == slot_floats else None
 
 
 def _merge_stacked(parts: torch.Tensor, D: int, out_dtype: torch.dtype) -> torch.Tensor:

@@ -44,7 +44,8 @@ enum cea_device_error {
   CEA_DEV_TIMEOUT_PRODUCER = 0x101,
   CEA_DEV_TIMEOUT_MMA = 0x102,
   CEA_DEV_TIMEOUT_SOFTMAX = 0x103,
-  CEA_DEV_TIMEOUT_DECODE = 0x104
+  CEA_DEV_TIMEOUT_DECODE = 0x104,
+  CEA_DEV_TIMEOUT_PEER = 0x105
 };
 
 typedef enum cea_dtype { CEA_F32 = 0, CEA_F16 = 1, CEA_BF16 = 2, CEA_F64 = 3 } cea_dtype;
@@ -222,6 +223,47 @@ int cea_alltoallv(cea_nccl_comm* comm, const void* send, const size_t* send_byte
                   void* recv, const size_t* recv_bytes, const size_t* recv_offsets, void* stream);
 /* recv (nranks * bytes) receives every rank's `bytes` bytes in rank order. */
 int cea_allgather(cea_nccl_comm* comm, const void* send, void* recv, size_t bytes, void* stream);
+
+/*
+ * Distributed-KV decode exchange over peer memory: the all-gather of the
+ * per-rank partials and their exact merge in one kernel, replacing the
+ * all-gather + list merge of collab_infer parallel/sequence_parallel.py:270-276
+ * (distributed_kv_attention) for ranks of one node (NVLink P2P).
+ *
+ * Every rank owns a receive buffer of 2 x nranks slots of rows * W floats (a
+ * row: partial output in columns [0, D), its natural-log lse in column D,
+ * padding; W a multiple of 4 greater than D) and nranks uint64 counters set to
+ * zero, and maps every peer's buffer and counters into its address space
+ * (cea_ipc_export / cea_ipc_open).  Call number `epoch` (1, 2, ... on these
+ * buffers, the same on every rank) uses slot parity epoch & 1: the caller
+ * first writes its own partial into slot [epoch & 1][rank] of its own buffer
+ * (cea_attn_fwd or cea_decode_splitkv with out / lse pointing there), then
+ * calls cea_peer_merge, which stores that slot into every peer's buffer,
+ * signals every peer through its counters, waits (bounded) for every peer's
+ * data and writes the merged [B, Sq, H, D] output.  Every rank must make the
+ * same sequence of calls; a wait that expires records CEA_DEV_TIMEOUT_PEER.
+ */
+#define CEA_MAX_PEERS 16
+typedef struct cea_peer_merge_params {
+  int32_t n, rank;
+  float* bufs[CEA_MAX_PEERS];      /* rank q's receive buffer as mapped in this process */
+  uint64_t* flags[CEA_MAX_PEERS];  /* rank q's nranks counters as mapped in this process */
+  uint64_t epoch;
+  int32_t B, Sq, H, D, W;
+  void* out;
+  int64_t o_stride[3]; /* b, s, h */
+  int32_t out_dtype;   /* F32, BF16 or F16 */
+} cea_peer_merge_params;
+
+int cea_peer_merge(const cea_peer_merge_params* p, void* stream);
+
+/* CUDA IPC of device memory between the processes of one node: the 64-byte
+ * handle of the allocation holding `ptr`, and ptr's offset in it. */
+#define CEA_IPC_HANDLE_BYTES 64
+int cea_ipc_export(const void* ptr, void* handle_out, size_t* offset_out);
+/* Maps a peer's allocation on the current device; *ptr_out = base + offset, *base_out for cea_ipc_close. */
+int cea_ipc_open(const void* handle, size_t offset, void** ptr_out, void** base_out);
+int cea_ipc_close(void* base);
 
 /* Reads (and with clear != 0 resets) the device error word of the current device. Synchronises `stream`. */
 int cea_device_status(int* status_out, int clear, void* stream);

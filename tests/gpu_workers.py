@@ -130,3 +130,35 @@ def nccl_abi_worker(rank, world):
     res["allgather"] = torch.equal(full, torch.arange(world, device=dev).repeat_interleave(333).to(torch.uint8) + 7)
     assert lib.cea_nccl_comm_destroy(comm) == 0, lib.cea_last_error()
     return res
+
+
+def peer_decode_worker(rank, world, T, B, Hq, Hkv, D):
+    """Distributed-KV decode through the peer-memory exchange, three calls in a row (slot parities 1, 0, 1 and
+    counters growing per call), against the all-gather path on the same inputs; also reports whether the
+    peer path was taken."""
+    import os
+
+    import collaborative_edge_system_b200 as cea
+    from collaborative_edge_system_b200 import _lib
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    lay = cea.SequenceLayout(T, world)
+    res = []
+    for call in range(3):
+        g = torch.Generator().manual_seed(100 + call)
+        q = torch.randn(B, 1, Hq, D, generator=g).to(torch.bfloat16).to(dev)
+        k = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+        v = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+        kp = torch.arange(T).repeat(B, 1)
+        qp = torch.full((B, 1), T + call, device=dev)
+        kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (k, v, kp))
+        os.environ["CEA_PEER_DECODE"] = "1"
+        fast = cea.distributed_kv_attention(q, kl, vl, qp, pl, ctx.sp)
+        os.environ["CEA_PEER_DECODE"] = "0"
+        slow = cea.distributed_kv_attention(q, kl, vl, qp, pl, ctx.sp)
+        os.environ["CEA_PEER_DECODE"] = "1"
+        torch.cuda.synchronize(dev)
+        res.append(bool(torch.equal(fast, slow)))
+    pd = getattr(ctx.sp, "_cea_peer_decode", None)
+    return res, bool(pd is not None and pd.ok), _lib.device_status(clear=True, device=dev)

@@ -62,6 +62,13 @@ def test_nccl_entry_points_reject_bad_arguments_without_nccl_or_gpu():
     assert lib.cea_allgather(None, None, None, 16, None) == _lib.CEA_ERR_INVALID
     assert lib.cea_nccl_comm_destroy(None) == _lib.CEA_OK
     assert lib.cea_nccl_abort(None) == _lib.CEA_OK
+    pm = _lib.PeerMergeParams()
+    pm.n, pm.rank, pm.epoch = 17, 0, 1  # more ranks than the peer table holds
+    assert lib.cea_peer_merge(ctypes.byref(pm), None) == _lib.CEA_ERR_INVALID
+    pm.n, pm.epoch = 2, 0
+    assert lib.cea_peer_merge(ctypes.byref(pm), None) == _lib.CEA_ERR_INVALID
+    assert lib.cea_ipc_export(None, None, None) == _lib.CEA_ERR_INVALID
+    assert lib.cea_ipc_close(None) == _lib.CEA_OK
 
 
 def test_product_path_refuses_cpu_tensors():
@@ -90,6 +97,9 @@ int main(void) {
   P(cea_segment, nh);
   printf("cea_copy_params %zu\n", sizeof(cea_copy_params));
   P(cea_copy_params, seg);
+  printf("cea_peer_merge_params %zu\n", sizeof(cea_peer_merge_params));
+  P(cea_peer_merge_params, flags); P(cea_peer_merge_params, epoch); P(cea_peer_merge_params, W);
+  P(cea_peer_merge_params, out); P(cea_peer_merge_params, out_dtype);
   return 0;
 }
 """
@@ -110,9 +120,11 @@ def test_struct_layout_matches_ctypes():
     assert c["cea_merge_params"] == ctypes.sizeof(_lib.MergeParams)
     assert c["cea_segment"] == ctypes.sizeof(_lib.Segment)
     assert c["cea_copy_params"] == ctypes.sizeof(_lib.CopyParams)
+    assert c["cea_peer_merge_params"] == ctypes.sizeof(_lib.PeerMergeParams)
     for key, val in c.items():
         if "." in key:
             struct, field = key.split(".")
             cls = {"cea_attn_params": _lib.AttnParams, "cea_merge_params": _lib.MergeParams,
-                   "cea_segment": _lib.Segment, "cea_copy_params": _lib.CopyParams}[struct]
+                   "cea_segment": _lib.Segment, "cea_copy_params": _lib.CopyParams,
+                   "cea_peer_merge_params": _lib.PeerMergeParams}[struct]
             assert getattr(cls, field).offset == val, key

@@ -45,3 +45,11 @@ def test_libcea_nccl_entry_points():
     """The C ABI's own NCCL communicator (for callers without a torch process group) moves the same bytes."""
     for res in _run(W.nccl_abi_worker, 2):
         assert res == {"ring": True, "alltoallv": True, "allgather": True}, res
+
+
+def test_peer_memory_decode_merge_matches_all_gather_path():
+    """The one-kernel exchange and merge over peer memory gives the same decode output as all-gather + merge."""
+    for res, used, status in _run(W.peer_decode_worker, 2, 3000, 4, 8, 2, 128):
+        assert used, "peer-memory exchange was not set up"
+        assert res == [True, True, True], res
+        assert status == 0
