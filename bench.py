@@ -575,7 +575,7 @@ def main():
                                      "cache_tokens": DEC_T, "sharding": "contiguous"},
                           "roofline": {"bound": "hbm", "kernel": "decode_partial_kernel", "achieved": dec["kernel_gbs"],
                                        "peak": hbm, "unit": "GB/s", "frac": dec["hbm_frac"],
-                                       "traffic": traffic.get("decode_partial_kernel_bytes_per_launch"),
+                                       "traffic": traffic.get("decode_partial_kernel_bytes_per_launch") if world == 1 else None,
                                        "kernel_ms": dec["kernel_ms"]}}
     if uly is not None:
         line["ulysses"] = uly

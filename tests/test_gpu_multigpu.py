@@ -29,14 +29,23 @@ def test_ring_attention_nccl(kind, weights, S, pad):
         assert stats["sp.send"]["calls"] == 1
 
 
+@pytest.mark.parametrize("world", [4, 8])
+def test_ring_attention_nccl_wide(world):
+    """Zigzag ring over more ranks: world - 1 grouped ring steps per rank."""
+    for eo, el, stats in _run(W.ring_worker, world, "zigzag", None, 2048, 8, 2, 128, 0):
+        assert eo < 2e-2 and el < 1e-3, (eo, el)
+        assert stats["sp.send"]["calls"] == world - 1
+
+
 def test_ulysses_attention_nccl():
     for eo, ek in _run(W.ulysses_worker, 2, [3, 1], 512, 8, 8, 128):
         assert eo < 2e-2
         assert ek == 0.0
 
 
-def test_distributed_kv_decode_nccl():
-    for eo, dtype in _run(W.decode_worker, 2, 3000, 4, 8, 2, 128):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_distributed_kv_decode_nccl(world):
+    for eo, dtype in _run(W.decode_worker, world, 3000, 4, 8, 2, 128):
         assert eo < 2e-2
         assert dtype == "torch.bfloat16"
 
@@ -47,9 +56,10 @@ def test_libcea_nccl_entry_points():
         assert res == {"ring": True, "alltoallv": True, "allgather": True}, res
 
 
-def test_peer_memory_decode_merge_matches_all_gather_path():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_memory_decode_merge_matches_all_gather_path(world):
     """The one-kernel exchange and merge over peer memory gives the same decode output as all-gather + merge."""
-    for res, used, status in _run(W.peer_decode_worker, 2, 3000, 4, 8, 2, 128):
+    for res, used, status in _run(W.peer_decode_worker, world, 3000, 4, 8, 2, 128):
         assert used, "peer-memory exchange was not set up"
         assert res == [True, True, True], res
         assert status == 0
