@@ -349,19 +349,41 @@ def bench_ulysses(cea, rank, world, dev, steps, warmup):
 
 # ----------------------------------------------------------------------------- ours: decode
 def bench_decode(cea, rank, world, dev):
+    """Config 4 through the distributed KV cache, as the engine drives it (engine.py:235-244, llama.py:250-256).
+
+    Every rank's 131072/N-token shard enters its ``LayerKVCache`` through one ``cea_kv_append`` (timed on its
+    own as the ``kv_append`` side metric); each decode step hands the new token to the least-loaded rank
+    (``assign_tokens``), which appends it, and every rank attends to its shard with the partials merged
+    across the SP group (``ring_decode_attention``).  The cache reserves room for every step, so nothing
+    grows inside the timed region.
+    """
     from collaborative_edge_system_b200 import _lib
+    from collaborative_edge_system_b200.cache import KVCache, assign_tokens, ring_decode_attention
 
     T_loc = [DEC_T // world + (1 if r < DEC_T % world else 0) for r in range(world)]
     start_pos = sum(T_loc[:rank])
-    cap = T_loc[rank] + (DEC_STEPS + DEC_WARM if rank == world - 1 else 0)
     g = torch.Generator(device=dev).manual_seed(99 + rank)
-    kc = torch.randn(DEC_B, HKV, cap, D, generator=g, device=dev).to(torch.bfloat16)  # head-major cache
-    vc = torch.randn(DEC_B, HKV, cap, D, generator=g, device=dev).to(torch.bfloat16)
-    kpos = torch.full((DEC_B, cap), -1, dtype=torch.int64, device=dev)
-    kpos[:, : T_loc[rank]] = torch.arange(start_pos, start_pos + T_loc[rank], device=dev)
     comm = cea.ParallelContext(1, world, 1, device=dev).sp
-    length = T_loc[rank]
-    owner = world - 1
+    kv = KVCache(reserve_tokens=DEC_STEPS + DEC_WARM)
+    layer = kv.layer(0)
+    assign_tokens(kv, DEC_T, world, sharded_sizes=T_loc)
+    # the prefill shard, token-major as the attention layer produces it
+    k_tok = torch.randn(DEC_B, T_loc[rank], HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    v_tok = torch.randn(DEC_B, T_loc[rank], HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    p_tok = torch.arange(start_pos, start_pos + T_loc[rank], device=dev).repeat(DEC_B, 1)
+    layer.append(k_tok, v_tok, p_tok)
+    # the shard append alone, rewritten into the same slots (inputs far larger than L2)
+    app_ev = []
+    for _ in range(3):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        _lib.kv_append(k_tok, v_tok, p_tok, layer.k, layer.v, layer.pos, 0)
+        e.record()
+        app_ev.append((s, e))
+    torch.cuda.synchronize(dev)
+    app_ms = min(s.elapsed_time(e) for s, e in app_ev)
+    app_bytes = 2.0 * (k_tok.numel() + v_tok.numel()) * 2 + 2.0 * p_tok.numel() * 8
+    del k_tok, v_tok, p_tok
     scale = 1.0 / math.sqrt(D)
     ev = []
     orig = _lib.attn_fwd
@@ -373,22 +395,19 @@ def bench_decode(cea, rank, world, dev):
         e.record()
         ev.append((s, e))
 
-    state = {"length": length, "pos": DEC_T, "i": 0}
+    state = {"pos": DEC_T, "i": 0, "mine": 0}
     qs = torch.randn(8, DEC_B, 1, HQ, D, generator=g, device=dev).to(torch.bfloat16)
-    kvs = torch.randn(8, DEC_B, HKV, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    kvs = torch.randn(8, DEC_B, 1, HKV, D, generator=g, device=dev).to(torch.bfloat16)
 
     def step():
-        L = state["length"]
+        owner = assign_tokens(kv, 1, world)  # same decision on every rank, no message
         qpos = torch.full((DEC_B, 1), state["pos"], dtype=torch.int64, device=dev)
         i = state["i"] = (state["i"] + 1) % 8
-        q = qs[i]
-        if rank == owner:  # the new token's K/V join the last rank's shard
-            kc[:, :, L : L + 1] = kvs[i]
-            vc[:, :, L : L + 1] = kvs[(i + 3) % 8]
-            kpos[:, L] = state["pos"]
-            state["length"] = L = L + 1
-        k_view, v_view = kc[:, :, :L].transpose(1, 2), vc[:, :, :L].transpose(1, 2)
-        out = cea.distributed_kv_attention(q, k_view, v_view, qpos, kpos[:, :L], comm, causal=True, scale=scale)
+        mine = owner == rank or world == 1
+        new_k, new_v = (kvs[i], kvs[(i + 3) % 8]) if mine else (None, None)
+        state["mine"] += mine
+        out = ring_decode_attention(qs[i], new_k, new_v, qpos, layer, comm, owner, causal=True, scale=scale,
+                                    num_kv_heads=HKV)
         state["pos"] += 1
         return out
 
@@ -396,6 +415,7 @@ def bench_decode(cea, rank, world, dev):
         step()
     barrier(world)
     _lib.attn_fwd = timed_fwd
+    state["mine"] = 0
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(DEC_STEPS):
@@ -405,7 +425,7 @@ def bench_decode(cea, rank, world, dev):
     _lib.attn_fwd = orig
     ms = max_over_ranks(t0.elapsed_time(t1), world, dev)
     kern_ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
-    avg_len = state["length"] - DEC_STEPS / 2 if rank == owner else state["length"]
+    avg_len = len(layer) - state["mine"] / 2
     kv_bytes = 2.0 * DEC_B * HKV * avg_len * D * 2  # K and V read by this rank per step
     hbm = _peaks()[2]
     return {
@@ -415,6 +435,10 @@ def bench_decode(cea, rank, world, dev):
         "kernel_gbs": kv_bytes / (kern_ms / 1e3) / 1e9,
         "hbm_frac": kv_bytes / (kern_ms / 1e3) / 1e9 / hbm,
         "kv_bytes_per_step_rank": kv_bytes,
+        "append": {"kernel": "kv_append_kernel", "tokens": T_loc[rank], "ms": app_ms, "bytes": app_bytes,
+                   "gbs": app_bytes / (app_ms / 1e3) / 1e9, "frac": app_bytes / (app_ms / 1e3) / 1e9 / hbm,
+                   "peak": hbm},
+        "sp_lengths": list(kv.sp_lengths) if kv.sp_lengths is not None else [len(layer)],
     }
 
 
@@ -576,7 +600,15 @@ def main():
                           "roofline": {"bound": "hbm", "kernel": "decode_partial_kernel", "achieved": dec["kernel_gbs"],
                                        "peak": hbm, "unit": "GB/s", "frac": dec["hbm_frac"],
                                        "traffic": traffic.get("decode_partial_kernel_bytes_per_launch") if world == 1 else None,
-                                       "kernel_ms": dec["kernel_ms"]}}
+                                       "kernel_ms": dec["kernel_ms"]},
+                          "cache": {"owner": "least-loaded SP rank per token", "sp_lengths": dec["sp_lengths"]}}
+        a = dec["append"]
+        line["kv_append"] = {"metric": "KV-cache shard append GB/s (per rank)", "value": a["gbs"], "unit": "GB/s",
+                             "config": {"batch": DEC_B, "tokens": a["tokens"], "kv_heads": HKV, "head_dim": D,
+                                        "dtype": "bf16"},
+                             "roofline": {"bound": "hbm", "kernel": a["kernel"], "achieved": a["gbs"], "peak": a["peak"],
+                                          "unit": "GB/s", "frac": a["frac"], "bytes_per_launch": a["bytes"],
+                                          "kernel_ms": a["ms"]}}
     if uly is not None:
         line["ulysses"] = uly
     if rank == 0 and world == 1 and not args.no_cpu:

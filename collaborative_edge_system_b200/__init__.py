@@ -20,6 +20,7 @@ from .attention import (
     merge_attention_list,
     visibility_mask,
 )
+from .cache import KVCache, LayerKVCache, assign_tokens, ring_decode_attention
 from .comm import CommStats, CommWork, Communicator, NetworkConfig, NetworkEmulator, dist_ready
 from .launcher import init_distributed, launch_local
 from .mesh import ParallelContext
@@ -40,11 +41,14 @@ __all__ = [
     "CommWork",
     "Communicator",
     "HeadShard",
+    "KVCache",
+    "LayerKVCache",
     "NetworkConfig",
     "NetworkEmulator",
     "ParallelContext",
     "SequenceLayout",
     "accumulation_dtype",
+    "assign_tokens",
     "attend_into",
     "attention",
     "attention_with_lse",
@@ -63,6 +67,7 @@ __all__ = [
     "offsets_of",
     "partition_heads",
     "ring_attention",
+    "ring_decode_attention",
     "shard_sequence",
     "split_sizes",
     "ulysses_attention",

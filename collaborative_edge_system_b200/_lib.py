@@ -20,7 +20,7 @@ F32, F16, BF16, F64 = 0, 1, 2, 3
 _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
 
 CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE, CEA_ERR_NCCL = range(7)
-ABI_VERSION = 2
+ABI_VERSION = 3
 NCCL_ID_BYTES = 128
 MAX_PEERS = 16
 IPC_HANDLE_BYTES = 64
@@ -126,6 +126,36 @@ class CopyParams(ctypes.Structure):
     ]
 
 
+_i64x2 = ctypes.c_int64 * 2
+
+
+class KvAppendParams(ctypes.Structure):
+    _fields_ = [
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("k_stride", _i64x3),
+        ("v_stride", _i64x3),
+        ("kc_stride", _i64x3),
+        ("vc_stride", _i64x3),
+        ("pos", ctypes.c_void_p),
+        ("pos_stride", _i64x2),
+        ("pos_cache", ctypes.c_void_p),
+        ("pc_stride", _i64x2),
+        ("B", ctypes.c_int32),
+        ("n", ctypes.c_int32),
+        ("Hk", ctypes.c_int32),
+        ("Dk", ctypes.c_int32),
+        ("Hv", ctypes.c_int32),
+        ("Dv", ctypes.c_int32),
+        ("k_elem_bytes", ctypes.c_int32),
+        ("v_elem_bytes", ctypes.c_int32),
+        ("offset", ctypes.c_int64),
+        ("capacity", ctypes.c_int64),
+    ]
+
+
 EXPORTS = (
     "cea_attn_fwd",
     "cea_attn_workspace_size",
@@ -135,6 +165,7 @@ EXPORTS = (
     "cea_merge",
     "cea_ulysses_pack",
     "cea_ulysses_unpack",
+    "cea_kv_append",
     "cea_device_status",
     "cea_last_error",
     "cea_abi_version",
@@ -177,6 +208,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             ("cea_merge", [ctypes.POINTER(MergeParams), P], ctypes.c_int),
             ("cea_ulysses_pack", [ctypes.POINTER(CopyParams), P], ctypes.c_int),
             ("cea_ulysses_unpack", [ctypes.POINTER(CopyParams), P], ctypes.c_int),
+            ("cea_kv_append", [ctypes.POINTER(KvAppendParams), P], ctypes.c_int),
             ("cea_device_status", [ctypes.POINTER(ctypes.c_int), ctypes.c_int, P], ctypes.c_int),
             ("cea_last_error", [], ctypes.c_char_p),
             ("cea_abi_version", [], ctypes.c_int),
@@ -390,6 +422,41 @@ def copy_segments(segments, D: int, elem_bytes: int, device: torch.device, entry
             s.dst_stride = _i64x3(dst.stride(0), dst.stride(1), dst.stride(2))
             s.nb, s.ns, s.nh = src.shape[0], src.shape[1], src.shape[2]
         _check(fn(ctypes.byref(p), _stream_ptr(device)), entry)
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, pos: Optional[torch.Tensor], k_cache: torch.Tensor,
+              v_cache: torch.Tensor, pos_cache: Optional[torch.Tensor], offset: int) -> None:
+    """cea_kv_append: token-major ``k``/``v`` ``[B, n, H, D]`` (and ``pos`` ``[B, n]``) into the head-major
+    ``k_cache``/``v_cache`` ``[B, H, cap, D]`` (and ``pos_cache`` ``[B, cap]``) at token slot ``offset``."""
+    require_cuda(k, v, k_cache, v_cache, pos, pos_cache)
+    for t in (k, v, k_cache, v_cache):
+        if t.dim() != 4 or t.stride(3) != 1:
+            raise ValueError("k, v and the cache buffers must be 4-D with a contiguous last dimension")
+    if (pos is None) != (pos_cache is None):
+        raise ValueError("positions need both the source and the cache tensor")
+    p = KvAppendParams()
+    p.k, p.v, p.k_cache, p.v_cache = k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr()
+    p.k_stride = _i64x3(k.stride(0), k.stride(1), k.stride(2))
+    p.v_stride = _i64x3(v.stride(0), v.stride(1), v.stride(2))
+    p.kc_stride = _i64x3(k_cache.stride(0), k_cache.stride(2), k_cache.stride(1))
+    p.vc_stride = _i64x3(v_cache.stride(0), v_cache.stride(2), v_cache.stride(1))
+    if pos is not None:
+        if pos.dtype != torch.int64 or pos_cache.dtype != torch.int64:
+            raise ValueError("positions must be int64")
+        p.pos, p.pos_cache = pos.data_ptr(), pos_cache.data_ptr()
+        p.pos_stride = _i64x2(pos.stride(0), pos.stride(1))
+        p.pc_stride = _i64x2(pos_cache.stride(0), pos_cache.stride(1))
+    p.B, p.n, p.Hk, p.Dk = k.shape[0], k.shape[1], k.shape[2], k.shape[3]
+    p.Hv, p.Dv = v.shape[2], v.shape[3]
+    p.k_elem_bytes, p.v_elem_bytes = k.element_size(), v.element_size()
+    p.offset, p.capacity = int(offset), k_cache.shape[2]
+    if (k_cache.shape[0], k_cache.shape[1], k_cache.shape[3]) != (p.B, p.Hk, p.Dk) or v_cache.shape[2] != p.capacity \
+            or (v_cache.shape[0], v_cache.shape[1], v_cache.shape[3]) != (p.B, p.Hv, p.Dv) or v.shape[:2] != k.shape[:2]:
+        raise ValueError(f"cache buffers {tuple(k_cache.shape)}/{tuple(v_cache.shape)} do not hold "
+                         f"k {tuple(k.shape)} / v {tuple(v.shape)}")
+    if k.dtype != k_cache.dtype or v.dtype != v_cache.dtype:
+        raise ValueError("k/v and the cache buffers must share a dtype")
+    _check(load().cea_kv_append(ctypes.byref(p), _stream_ptr(k_cache.device)), "cea_kv_append")
 
 
 def device_status(clear: bool = True, device: Optional[torch.device] = None) -> int:

@@ -16,6 +16,7 @@
 #include "cea_common.cuh"
 #include "cea_nccl.cuh"
 #include "decode.cuh"
+#include "kv_cache.cuh"
 #include "peer_merge.cuh"
 
 using namespace cea;
@@ -686,6 +687,63 @@ static int copy_segments(const cea_copy_params* p, void* stream, const char* wha
 
 int cea_ulysses_pack(const cea_copy_params* p, void* stream) { return copy_segments(p, stream, "cea_ulysses_pack"); }
 int cea_ulysses_unpack(const cea_copy_params* p, void* stream) { return copy_segments(p, stream, "cea_ulysses_unpack"); }
+
+int cea_kv_append(const cea_kv_append_params* p, void* stream) {
+  const char* what = "cea_kv_append";
+  if (p == nullptr) return fail(CEA_ERR_INVALID, "%s: null params", what);
+  if (p->B < 0 || p->n < 0) return fail(CEA_ERR_INVALID, "%s: B and n must be >= 0", what);
+  if (p->Hk < 1 || p->Dk < 1 || p->Hv < 1 || p->Dv < 1) return fail(CEA_ERR_INVALID, "%s: heads and head dims must be >= 1", what);
+  if (p->offset < 0 || p->capacity < 0 || p->offset + p->n > p->capacity)
+    return fail(CEA_ERR_INVALID, "%s: slots %lld..%lld outside a capacity of %lld", what, (long long)p->offset,
+                (long long)(p->offset + p->n), (long long)p->capacity);
+  const int eb[2] = {p->k_elem_bytes, p->v_elem_bytes};
+  for (int i = 0; i < 2; ++i)
+    if (eb[i] != 1 && eb[i] != 2 && eb[i] != 4 && eb[i] != 8) return fail(CEA_ERR_INVALID, "%s: element size %d", what, eb[i]);
+  if ((p->pos == nullptr) != (p->pos_cache == nullptr))
+    return fail(CEA_ERR_INVALID, "%s: positions need both the source and the cache pointer", what);
+  if (static_cast<int64_t>(p->B) * p->n == 0) return CEA_OK;
+  if (!p->k || !p->v || !p->k_cache || !p->v_cache) return fail(CEA_ERR_INVALID, "%s: null k/v pointer", what);
+  cea::kvc::Args a{};
+  const void* src[2] = {p->k, p->v};
+  void* dst[2] = {p->k_cache, p->v_cache};
+  const int64_t* ss[2] = {p->k_stride, p->v_stride};
+  const int64_t* ds[2] = {p->kc_stride, p->vc_stride};
+  const int H[2] = {p->Hk, p->Hv}, D[2] = {p->Dk, p->Dv};
+  int64_t most = static_cast<int64_t>(p->B) * p->n;
+  for (int i = 0; i < 2; ++i) {
+    cea::kvc::Tensor& t = a.t[i];
+    t.src = static_cast<const uint8_t*>(src[i]);
+    t.dst = static_cast<uint8_t*>(dst[i]);
+    t.H = H[i];
+    const int64_t row = static_cast<int64_t>(D[i]) * eb[i];
+    uint64_t align = reinterpret_cast<uintptr_t>(src[i]) | reinterpret_cast<uintptr_t>(dst[i]) | row;
+    for (int j = 0; j < 3; ++j) {
+      t.src_stride[j] = ss[i][j] * eb[i];
+      t.dst_stride[j] = ds[i][j] * eb[i];
+      align |= static_cast<uint64_t>(t.src_stride[j]) | static_cast<uint64_t>(t.dst_stride[j]);
+    }
+    int unit = 16;
+    while (unit > 1 && (align & (unit - 1))) unit >>= 1;
+    t.unit = unit;
+    t.units = static_cast<int>(row / unit);
+    const int64_t per_b = static_cast<int64_t>(p->n) * t.H * t.units;
+    if (per_b >= (int64_t(1) << 31)) return fail(CEA_ERR_UNSUPPORTED, "%s: %lld units per sequence", what, (long long)per_b);
+    most = std::max(most, per_b * p->B);
+  }
+  a.pos_src = p->pos;
+  a.pos_dst = p->pos_cache;
+  a.ps_b = p->pos_stride[0];
+  a.ps_s = p->pos_stride[1];
+  a.pd_b = p->pc_stride[0];
+  a.pd_t = p->pc_stride[1];
+  a.B = p->B;
+  a.n = p->n;
+  a.offset = p->offset;
+  const int64_t blocks = std::min<int64_t>((most + 255) / 256, 148 * 8);
+  cea::kvc::kv_append_kernel<<<dim3(static_cast<unsigned>(blocks), p->pos ? 3 : 2), 256, 0,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return cuda_check(what);
+}
 
 int cea_device_status(int* status_out, int clear, void* stream) {
   if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return cuda_check("cea_device_status");

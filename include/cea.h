@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define CEA_ABI_VERSION 2
+#define CEA_ABI_VERSION 3
 
 enum cea_status {
   CEA_OK = 0,
@@ -182,6 +182,39 @@ typedef struct cea_copy_params {
 
 int cea_ulysses_pack(const cea_copy_params* p, void* stream);
 int cea_ulysses_unpack(const cea_copy_params* p, void* stream);
+
+/*
+ * KV-cache append (collab_infer models/cache.py:51-62, LayerKVCache.append):
+ * copies n new tokens of token-major k [B, n, Hk, Dk] and v [B, n, Hv, Dv]
+ * into the head-major cache buffers [B, Hk, capacity, Dk] and
+ * [B, Hv, capacity, Dv] at token slots offset .. offset + n - 1, and their
+ * positions [B, n] (int64) into the cache's positions [B, capacity], in one
+ * launch.  The same call moves the cached tokens into a grown buffer
+ * (cache.py:39-49: source = the old cache seen token-major, offset 0).
+ * Strides are in elements; the innermost (D) dimension is contiguous.  k and
+ * v are copied bit for bit (any dtype of 1, 2, 4 or 8 bytes); pos and
+ * pos_cache are both NULL to leave positions alone.  The ring-mode decode
+ * owner (engine/engine.py:235-244) is host logic and stays in the caller.
+ */
+typedef struct cea_kv_append_params {
+  const void* k;
+  const void* v;
+  void* k_cache;
+  void* v_cache;
+  int64_t k_stride[3];  /* source b, s, h */
+  int64_t v_stride[3];
+  int64_t kc_stride[3]; /* cache b, t, h */
+  int64_t vc_stride[3];
+  const int64_t* pos;
+  int64_t pos_stride[2]; /* source b, s */
+  int64_t* pos_cache;
+  int64_t pc_stride[2]; /* cache b, t */
+  int32_t B, n, Hk, Dk, Hv, Dv;
+  int32_t k_elem_bytes, v_elem_bytes;
+  int64_t offset, capacity;
+} cea_kv_append_params;
+
+int cea_kv_append(const cea_kv_append_params* p, void* stream);
 
 /*
  * NCCL transfers of the sequence-parallel path, for callers that hold no

@@ -24,3 +24,4 @@ from .attention_ref import (  # noqa: F401
     ulysses_attention,
     visibility,
 )
+from . import kv_cache  # noqa: F401,E402

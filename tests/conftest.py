@@ -33,3 +33,16 @@ def golden_single():
 @pytest.fixture(scope="session")
 def golden_sp():
     return load_golden("sequence_parallel.npz")
+
+
+@pytest.fixture(scope="session")
+def golden_cache():
+    return load_golden("kv_cache.npz")
+
+
+@pytest.fixture(scope="session")
+def golden_cache_engine():
+    import json
+
+    with open(os.path.join(GOLDEN, "kv_cache_engine.json")) as f:
+        return json.load(f)

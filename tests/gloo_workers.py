@@ -53,11 +53,55 @@ def install_oracle_compute():
         for src, dst in pairs:
             dst.copy_(src)
 
+    def copy_tokens(k_cache, v_cache, pos_cache, k, v, pos, offset):
+        n = k.shape[1]
+        k_cache[:, :, offset : offset + n] = k.transpose(1, 2)
+        v_cache[:, :, offset : offset + n] = v.transpose(1, 2)
+        if pos is not None:
+            pos_cache[:, offset : offset + n] = pos
+
+    import collaborative_edge_system_b200.cache as cache_mod
+
+    cache_mod._copy_tokens = copy_tokens
+    cache_mod._check_device = lambda *tensors: None
     sp.attend_into = attend_into
     sp.attention_with_lse = attention_with_lse
     sp.attention = attention
     sp._merge = merge
     sp._copy_segments = copy_segments
+
+
+def cached_decode_worker(rank, world, weights, prompt, steps):
+    """Ring-mode generate loop over the distributed KV cache (host logic; compute and copies by the oracle)."""
+    install_oracle_compute()
+    from collaborative_edge_system_b200 import ParallelContext, SequenceLayout
+    from collaborative_edge_system_b200.cache import KVCache, assign_tokens, ring_decode_attention
+
+    ctx = ParallelContext(1, world, 1)
+    B, Hq, Hkv, D, T = 2, 4, 2, 8, prompt + steps
+    g = torch.Generator().manual_seed(prompt)
+    k_all = torch.randn(B, T, Hkv, D, generator=g, dtype=torch.float64)
+    v_all = torch.randn(B, T, Hkv, D, generator=g, dtype=torch.float64)
+    qs = torch.randn(steps, B, 1, Hq, D, generator=g, dtype=torch.float64)
+    pos_all = torch.arange(T).repeat(B, 1)
+    pos_all[1, :2] = -1
+    kv = KVCache(reserve_tokens=1)
+    layer = kv.layer(0)
+    lay = SequenceLayout(prompt, world, weights, "contiguous")
+    assign_tokens(kv, prompt, world, sharded_sizes=lay.sizes)
+    layer.append(*(lay.shard(t[:, :prompt], rank) for t in (k_all, v_all, pos_all)))
+    errs, owners = [], []
+    for step in range(steps):
+        t = prompt + step
+        owner = assign_tokens(kv, 1, world)
+        owners.append(owner)
+        sl = slice(t, t + 1)
+        new = (k_all[:, sl], v_all[:, sl]) if owner == rank else (None, None)
+        out = ring_decode_attention(qs[step], *new, pos_all[:, sl], layer, ctx.sp, owner, num_kv_heads=Hkv)
+        ref = oracle.attention(qs[step].numpy(), k_all[:, : t + 1].numpy(), v_all[:, : t + 1].numpy(),
+                               pos_all[:, sl].numpy(), pos_all[:, : t + 1].numpy(), True)
+        errs.append(float(np.abs(out.numpy() - ref).max()))
+    return max(errs), owners, kv.sp_lengths, len(layer), layer.capacity
 
 
 def golden_inputs():

@@ -162,3 +162,48 @@ def peer_decode_worker(rank, world, T, B, Hq, Hkv, D):
         res.append(bool(torch.equal(fast, slow)))
     pd = getattr(ctx.sp, "_cea_peer_decode", None)
     return res, bool(pd is not None and pd.ok), _lib.device_status(clear=True, device=dev)
+
+
+def cached_decode_worker(rank, world, prompt, steps, B, Hq, Hkv, D, weights):
+    """The ring-mode generate loop over a distributed KV cache (engine.py:235-244, llama.py:236-256):
+    a sharded prefill appends every rank's shard, then each decode step hands the new token to the
+    least-loaded rank (assign_tokens), which appends it with the CUDA append kernel; every rank attends
+    to its shard and the partials merge.  Each step's output is checked against attention over the
+    whole history, and the per-rank cache contents against the tokens this rank should hold."""
+    import collaborative_edge_system_b200 as cea
+    from collaborative_edge_system_b200.cache import KVCache, assign_tokens, ring_decode_attention
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    T = prompt + steps
+    g = torch.Generator().manual_seed(41 + prompt)
+    k_all = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+    v_all = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+    qs = torch.randn(steps, B, 1, Hq, D, generator=g).to(torch.bfloat16)
+    pos_all = torch.arange(T).repeat(B, 1)
+    pos_all[1:, :3] = -1  # left padding of the shorter sequences is cached like any token
+    kv = KVCache(reserve_tokens=2)
+    layer = kv.layer(0)
+    lay = cea.SequenceLayout(prompt, world, weights, "contiguous")
+    assign_tokens(kv, prompt, world, sharded_sizes=lay.sizes)
+    mine = [int(i) for i in lay.indices(rank)]
+    layer.append(*(lay.shard(t[:, :prompt], rank).to(dev) for t in (k_all, v_all, pos_all)))
+    errs, owners = [], []
+    for step in range(steps):
+        t = prompt + step
+        owner = assign_tokens(kv, 1, world)
+        owners.append(owner)
+        if owner == rank:
+            mine.append(t)
+        sl = slice(t, t + 1)
+        q = qs[step].to(dev)
+        new_k, new_v = (x[:, sl].to(dev) for x in (k_all, v_all)) if owner == rank else (None, None)
+        out = ring_decode_attention(q, new_k, new_v, pos_all[:, sl].to(dev), layer, ctx.sp, owner,
+                                    num_kv_heads=Hkv)
+        ref = oracle.attention(_np(qs[step]), _np(k_all[:, : t + 1]), _np(v_all[:, : t + 1]), pos_all[:, sl].numpy(),
+                               pos_all[:, : t + 1].numpy(), True)
+        errs.append(float(np.abs(_np(out) - ref).max()))
+    kc, vc, pc = layer.view()
+    held = (torch.equal(kc.cpu(), k_all[:, mine]) and torch.equal(vc.cpu(), v_all[:, mine])
+            and torch.equal(pc.cpu(), pos_all[:, mine]))
+    return max(errs), owners, kv.sp_lengths, held

@@ -29,7 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.cea_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.cea_abi_version() == _lib.ABI_VERSION == 3
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
@@ -71,6 +71,26 @@ def test_nccl_entry_points_reject_bad_arguments_without_nccl_or_gpu():
     assert lib.cea_ipc_close(None) == _lib.CEA_OK
 
 
+def test_kv_append_rejects_bad_arguments_without_a_gpu():
+    lib = _lib.load()
+    assert lib.cea_kv_append(None, None) == _lib.CEA_ERR_INVALID
+    kp = _lib.KvAppendParams()
+    kp.B, kp.n, kp.Hk, kp.Dk, kp.Hv, kp.Dv = 1, 4, 2, 8, 2, 8
+    kp.k_elem_bytes = kp.v_elem_bytes = 2
+    kp.offset, kp.capacity = 2, 5  # slots 2..5 do not fit a capacity of 5
+    assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_ERR_INVALID
+    kp.offset = 1
+    assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_ERR_INVALID  # null k/v pointers
+    kp.k_elem_bytes = 3
+    assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_ERR_INVALID
+    kp.k_elem_bytes, kp.pos = 2, 64  # positions without a cache positions pointer
+    assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_ERR_INVALID
+    kp.pos, kp.Hv = None, 0
+    assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_ERR_INVALID
+    kp.Hv, kp.n = 2, 0  # nothing to copy: no launch, no pointer needed
+    assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_OK
+
+
 def test_product_path_refuses_cpu_tensors():
     import torch
 
@@ -100,6 +120,10 @@ int main(void) {
   printf("cea_peer_merge_params %zu\n", sizeof(cea_peer_merge_params));
   P(cea_peer_merge_params, flags); P(cea_peer_merge_params, epoch); P(cea_peer_merge_params, W);
   P(cea_peer_merge_params, out); P(cea_peer_merge_params, out_dtype);
+  printf("cea_kv_append_params %zu\n", sizeof(cea_kv_append_params));
+  P(cea_kv_append_params, kc_stride); P(cea_kv_append_params, pos); P(cea_kv_append_params, pc_stride);
+  P(cea_kv_append_params, B); P(cea_kv_append_params, v_elem_bytes); P(cea_kv_append_params, offset);
+  P(cea_kv_append_params, capacity);
   return 0;
 }
 """
@@ -121,10 +145,11 @@ def test_struct_layout_matches_ctypes():
     assert c["cea_segment"] == ctypes.sizeof(_lib.Segment)
     assert c["cea_copy_params"] == ctypes.sizeof(_lib.CopyParams)
     assert c["cea_peer_merge_params"] == ctypes.sizeof(_lib.PeerMergeParams)
+    assert c["cea_kv_append_params"] == ctypes.sizeof(_lib.KvAppendParams)
     for key, val in c.items():
         if "." in key:
             struct, field = key.split(".")
             cls = {"cea_attn_params": _lib.AttnParams, "cea_merge_params": _lib.MergeParams,
                    "cea_segment": _lib.Segment, "cea_copy_params": _lib.CopyParams,
-                   "cea_peer_merge_params": _lib.PeerMergeParams}[struct]
+                   "cea_peer_merge_params": _lib.PeerMergeParams, "cea_kv_append_params": _lib.KvAppendParams}[struct]
             assert getattr(cls, field).offset == val, key

@@ -76,3 +76,18 @@ def test_compressed_collectives(comm_dtype, tol):
         assert out["dtype"] == "torch.float32"
         for key in ("all_reduce", "all_gather", "reduce_scatter", "all_to_all"):
             assert out[key] < tol, (key, out[key])
+
+
+@pytest.mark.parametrize("world,weights", [(2, None), (3, [3, 2, 1])])
+def test_cached_ring_decode_host_flow(world, weights):
+    """Sharded prefill into the distributed KV cache, then decode steps owned by the least-loaded rank:
+    every rank agrees on the owners, the cache lengths add up and every step equals full-history attention."""
+    prompt, steps = 11, 7
+    res = _run(W.cached_decode_worker, world, weights, prompt, steps)
+    lay = SequenceLayout(prompt, world, weights, "contiguous")
+    for r, (err, owners, lengths, held, cap) in enumerate(res):
+        assert err < 1e-12, err
+        assert owners == res[0][1] and lengths == res[0][2]
+        assert held == lengths[r] == lay.sizes[r] + owners.count(r)
+        assert cap >= held
+    assert sum(res[0][2]) == prompt + steps

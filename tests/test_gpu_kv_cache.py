@@ -1,0 +1,151 @@
+"""KV-cache write path on the GPU: the cea_kv_append kernel behind LayerKVCache against the reference's own
+cache (golden vectors) and the numpy restatement, bit for bit, and the ring-mode cached decode loop over NCCL."""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import gpu_workers as W
+import oracle
+from collaborative_edge_system_b200 import launch_local
+from collaborative_edge_system_b200.cache import KVCache, LayerKVCache, assign_tokens, ring_decode_attention
+
+pytestmark = [pytest.mark.gpu, pytest.mark.timeout(300)]
+DEV = torch.device("cuda", 0) if torch.cuda.is_available() else None
+
+
+def _bits(t):
+    return t.view(torch.int16) if t.dtype == torch.bfloat16 else t
+
+
+@pytest.mark.parametrize("case", ["growth_f32", "ragged_reserve", "decode_like", "bf16_bits"])
+def test_append_matches_reference_cache(golden_cache, case):
+    c = golden_cache[case]
+    m = json.loads(str(c["meta"]))
+
+    def tensor(a):
+        t = torch.from_numpy(np.ascontiguousarray(a))
+        return t.view(torch.bfloat16) if m["dtype"] == "bfloat16" else t
+
+    k_in, v_in, p_in = tensor(c["k_in"]).to(DEV), tensor(c["v_in"]).to(DEV), torch.from_numpy(c["pos_in"]).to(DEV)
+    cache = LayerKVCache(m["reserve"])
+    caps, lens, start = [], [], 0
+    for n in m["counts"]:
+        cache.append(k_in[:, start : start + n], v_in[:, start : start + n], p_in[:, start : start + n])
+        start += n
+        caps.append(cache.capacity)
+        lens.append(len(cache))
+    assert caps == c["capacity"].tolist() and lens == c["length"].tolist()
+    kc, vc, pc = cache.view()
+    assert np.array_equal(_bits(kc.contiguous()).cpu().numpy(), c["k_view"])
+    assert np.array_equal(_bits(vc.contiguous()).cpu().numpy(), c["v_view"])
+    assert np.array_equal(pc.cpu().numpy(), c["pos_view"])
+    assert list(cache.k.shape) == c["k_storage_shape"].tolist()
+    assert cache.nbytes() == int(c["nbytes"])
+    # slots past the cached tokens keep position -1
+    assert (cache.pos[:, len(cache) :] == -1).all()
+
+
+DTYPES = [torch.bfloat16, torch.float16, torch.float32, torch.float64, torch.uint8]
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d).replace("torch.", ""))
+@pytest.mark.parametrize("D,Dv", [(128, 128), (80, 80), (20, 20), (3, 3), (1, 1), (64, 16)])
+@pytest.mark.parametrize("pad", [0, 5])
+def test_append_strided_sources_all_widths(dtype, D, Dv, pad):
+    """k/v as slices of a fused projection (non-contiguous; an odd row pitch with ``pad``), every copy width the
+    kernel picks (16, 8, 4, 2, 1 bytes), K and V of different head sizes; against the numpy restatement."""
+    B, H, counts, reserve = 2, 3, [7, 1, 1, 30, 0, 2, 1], 3
+    g = torch.Generator().manual_seed(D * 7 + Dv)
+    T = sum(counts)
+    fused = (torch.randn(B, T, H * (D + Dv) + pad, generator=g) * 50).to(dtype)
+    k_all = fused[..., : H * D].view(B, T, H, D)
+    v_all = fused[..., H * D : H * (D + Dv)].view(B, T, H, Dv)
+    pos = torch.arange(T).repeat(B, 1)
+    ref = oracle.kv_cache.LayerKVCache(reserve)
+    cache = LayerKVCache(reserve)
+    fused_d, pos_d = fused.to(DEV), pos.to(DEV)
+    kd = fused_d[..., : H * D].view(B, T, H, D)
+    vd = fused_d[..., H * D : H * (D + Dv)].view(B, T, H, Dv)
+    assert not kd.is_contiguous()
+    start = 0
+    for n in counts:
+        sl = slice(start, start + n)
+        cache.append(kd[:, sl], vd[:, sl], pos_d[:, sl])
+        ref.append(_bits(k_all[:, sl]).numpy(), _bits(v_all[:, sl]).numpy(), pos[:, sl].numpy())
+        start += n
+        assert cache.capacity == ref.capacity and len(cache) == len(ref)
+    kc, vc, pc = cache.view()
+    rk, rv, rp = ref.view()
+    assert np.array_equal(_bits(kc.cpu()).numpy(), rk) and np.array_equal(_bits(vc.cpu()).numpy(), rv)
+    assert np.array_equal(pc.cpu().numpy(), rp)
+
+
+def test_append_prefill_shard_full_size():
+    """A 16384-token bf16 shard (the per-rank prefill of a 131072-token sequence on 8 GPUs), 8 KV heads, D=128,
+    into a cache with decode headroom; then 300 single-token appends."""
+    B, n, H, D = 1, 16384, 8, 128
+    g = torch.Generator(device=DEV).manual_seed(5)
+    k = torch.randn(B, n, H, D, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(B, n, H, D, generator=g, device=DEV).to(torch.bfloat16)
+    pos = torch.arange(n, device=DEV).view(1, n)
+    cache = LayerKVCache(reserve=256)
+    cache.append(k, v, pos)
+    assert cache.capacity == n + 256
+    kc, vc, pc = cache.view()
+    assert torch.equal(kc, k) and torch.equal(vc, v) and torch.equal(pc, pos)
+    new_k = torch.randn(300, B, 1, H, D, generator=g, device=DEV).to(torch.bfloat16)
+    for i in range(300):
+        cache.append(new_k[i], new_k[i] * 2, torch.full((1, 1), n + i, device=DEV))
+    assert cache.capacity == int((n + 256) * 1.5)
+    kc, vc, pc = cache.view()
+    assert torch.equal(kc[:, :n], k) and torch.equal(kc[:, n:], new_k[:, :, 0].permute(1, 0, 2, 3))
+    assert torch.equal(vc[:, n:], (new_k * 2)[:, :, 0].permute(1, 0, 2, 3))
+    assert torch.equal(pc[0], torch.arange(n + 300, device=DEV))
+
+
+def test_ring_decode_attention_single_rank():
+    """One SP rank: the owner path of the cached decode step (append + attention over the cache)."""
+    import collaborative_edge_system_b200 as cea
+
+    ctx = cea.ParallelContext(1, 1, 1, device=DEV)
+    B, Hq, Hkv, D, P, steps = 2, 8, 2, 128, 300, 4
+    g = torch.Generator().manual_seed(9)
+    k = torch.randn(B, P + steps, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, P + steps, Hkv, D, generator=g).to(torch.bfloat16)
+    pos = torch.arange(P + steps).repeat(B, 1)
+    kv = KVCache()
+    layer = kv.layer(0)
+    layer.append(k[:, :P].to(DEV), v[:, :P].to(DEV), pos[:, :P].to(DEV))
+    for s in range(steps):
+        t = P + s
+        owner = assign_tokens(kv, 1, 1)
+        assert owner is None  # one SP rank: no owner, the rank caches every token
+        q = torch.randn(B, 1, Hq, D, generator=g).to(torch.bfloat16)
+        out = ring_decode_attention(q.to(DEV), k[:, t : t + 1].to(DEV), v[:, t : t + 1].to(DEV),
+                                    pos[:, t : t + 1].to(DEV), layer, ctx.sp, owner)
+        ref = oracle.attention(q.double().numpy(), k[:, : t + 1].double().numpy(), v[:, : t + 1].double().numpy(),
+                               pos[:, t : t + 1].numpy(), pos[:, : t + 1].numpy(), True)
+        assert out.dtype == torch.bfloat16
+        assert np.abs(out.double().cpu().numpy() - ref).max() < 2e-2
+    assert len(layer) == P + steps
+
+
+def _gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world,weights", [(2, None), (3, [3, 2, 1]), (4, None)])
+def test_cached_ring_decode_multi_gpu(world, weights):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    steps = 7
+    res = launch_local(W.cached_decode_worker, world, args=(1000, steps, 3, 8, 2, 128, weights), backend="nccl",
+                       return_results=True, timeout_s=120, env={"NCCL_NVLS_ENABLE": "0"})
+    for err, owners, lengths, held in res:
+        assert err < 2e-2, err
+        assert held
+        assert owners == res[0][1] and lengths == res[0][2]  # every rank reaches the same decisions
+    assert sum(res[0][2]) == 1000 + steps
