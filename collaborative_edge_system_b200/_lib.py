@@ -126,9 +126,6 @@ class CopyParams(ctypes.Structure):
     ]
 
 
-_i64x2 = ctypes.c_int64 * 2
-
-
 class KvAppendParams(ctypes.Structure):
     _fields_ = [
         ("k", ctypes.c_void_p),
@@ -456,7 +453,35 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, pos: Optional[torch.Tensor], k_c
                          f"k {tuple(k.shape)} / v {tuple(v.shape)}")
     if k.dtype != k_cache.dtype or v.dtype != v_cache.dtype:
         raise ValueError("k/v and the cache buffers must share a dtype")
-    _check(load().cea_kv_append(ctypes.byref(p), _stream_ptr(k_cache.device)), "cea_kv_append")
+    lib, stream = load(), _stream_ptr(k_cache.device)
+    # one launch moves fewer than 2^31 copy units; bound the bytes per call by that (a unit is >= 1 byte)
+    per_tok = max(p.Hk * p.Dk * p.k_elem_bytes, p.Hv * p.Dv * p.v_elem_bytes)
+    limit = (1 << 31) - 1
+    B, n = p.B, p.n
+    if B * n * per_tok <= limit:
+        _check(lib.cea_kv_append(ctypes.byref(p), stream), "cea_kv_append")
+        return
+    toks = max(1, limit // per_tok)
+    for b0, bn, s0, sn in _append_chunks(B, n, toks):
+        c = KvAppendParams.from_buffer_copy(p)
+        c.k, c.v = k[b0:, s0:].data_ptr(), v[b0:, s0:].data_ptr()
+        c.k_cache, c.v_cache = k_cache[b0:].data_ptr(), v_cache[b0:].data_ptr()
+        if pos is not None:
+            c.pos, c.pos_cache = pos[b0:, s0:].data_ptr(), pos_cache[b0:].data_ptr()
+        c.B, c.n, c.offset = bn, sn, int(offset) + s0
+        _check(lib.cea_kv_append(ctypes.byref(c), stream), "cea_kv_append")
+
+
+def _append_chunks(B: int, n: int, toks: int):
+    """``(b0, nb, s0, ns)`` pieces of a ``B x n`` token grid with at most ``toks`` tokens each."""
+    if toks >= n:
+        per = max(1, toks // n)
+        for b0 in range(0, B, per):
+            yield b0, min(per, B - b0), 0, n
+    else:
+        for b0 in range(B):
+            for s0 in range(0, n, toks):
+                yield b0, 1, s0, min(toks, n - s0)
 
 
 def device_status(clear: bool = True, device: Optional[torch.device] = None) -> int:

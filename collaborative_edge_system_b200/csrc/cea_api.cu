@@ -714,7 +714,6 @@ int cea_kv_append(const cea_kv_append_params* p, void* stream) {
     cea::kvc::Tensor& t = a.t[i];
     t.src = static_cast<const uint8_t*>(src[i]);
     t.dst = static_cast<uint8_t*>(dst[i]);
-    t.H = H[i];
     const int64_t row = static_cast<int64_t>(D[i]) * eb[i];
     uint64_t align = reinterpret_cast<uintptr_t>(src[i]) | reinterpret_cast<uintptr_t>(dst[i]) | row;
     for (int j = 0; j < 3; ++j) {
@@ -725,10 +724,16 @@ int cea_kv_append(const cea_kv_append_params* p, void* stream) {
     int unit = 16;
     while (unit > 1 && (align & (unit - 1))) unit >>= 1;
     t.unit = unit;
-    t.units = static_cast<int>(row / unit);
-    const int64_t per_b = static_cast<int64_t>(p->n) * t.H * t.units;
-    if (per_b >= (int64_t(1) << 31)) return fail(CEA_ERR_UNSUPPORTED, "%s: %lld units per sequence", what, (long long)per_b);
-    most = std::max(most, per_b * p->B);
+    const int64_t units = row / unit;
+    const int64_t per_b = static_cast<int64_t>(p->n) * H[i] * units;
+    if (per_b * p->B >= (int64_t(1) << 31))
+      return fail(CEA_ERR_UNSUPPORTED, "%s: %lld copy units in one call (split the append)", what,
+                  (long long)(per_b * p->B));
+    t.units = cea::kvc::make_fastdiv(static_cast<uint32_t>(units));
+    t.H = cea::kvc::make_fastdiv(static_cast<uint32_t>(H[i]));
+    t.per_b = cea::kvc::make_fastdiv(static_cast<uint32_t>(per_b));
+    t.total = static_cast<uint32_t>(per_b * p->B);
+    most = std::max(most, (per_b * p->B + cea::kvc::kUnroll - 1) / cea::kvc::kUnroll);
   }
   a.pos_src = p->pos;
   a.pos_dst = p->pos_cache;
@@ -739,8 +744,8 @@ int cea_kv_append(const cea_kv_append_params* p, void* stream) {
   a.B = p->B;
   a.n = p->n;
   a.offset = p->offset;
-  const int64_t blocks = std::min<int64_t>((most + 255) / 256, 148 * 8);
-  cea::kvc::kv_append_kernel<<<dim3(static_cast<unsigned>(blocks), p->pos ? 3 : 2), 256, 0,
+  const int64_t blocks = std::min<int64_t>((most + cea::kvc::kThreads - 1) / cea::kvc::kThreads, 148 * 8);
+  cea::kvc::kv_append_kernel<<<dim3(static_cast<unsigned>(blocks), p->pos ? 3 : 2), cea::kvc::kThreads, 0,
                                reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return cuda_check(what);
 }

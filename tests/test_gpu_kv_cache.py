@@ -84,13 +84,14 @@ def test_append_strided_sources_all_widths(dtype, D, Dv, pad):
 
 
 def test_append_prefill_shard_full_size():
-    """A 16384-token bf16 shard (the per-rank prefill of a 131072-token sequence on 8 GPUs), 8 KV heads, D=128,
-    into a cache with decode headroom; then 300 single-token appends."""
-    B, n, H, D = 1, 16384, 8, 128
+    """16384-token bf16 shards (the per-rank prefill of 131072-token sequences on 8 GPUs) of 4 sequences, 8 KV
+    heads, D=128 (256 MB per tensor, larger than L2), into a cache with decode headroom; then 300 single-token
+    appends.  The first launch here is the one profiled for the append kernel's DRAM traffic."""
+    B, n, H, D = 4, 16384, 8, 128
     g = torch.Generator(device=DEV).manual_seed(5)
     k = torch.randn(B, n, H, D, generator=g, device=DEV).to(torch.bfloat16)
     v = torch.randn(B, n, H, D, generator=g, device=DEV).to(torch.bfloat16)
-    pos = torch.arange(n, device=DEV).view(1, n)
+    pos = torch.arange(n, device=DEV).repeat(B, 1)
     cache = LayerKVCache(reserve=256)
     cache.append(k, v, pos)
     assert cache.capacity == n + 256
@@ -98,12 +99,12 @@ def test_append_prefill_shard_full_size():
     assert torch.equal(kc, k) and torch.equal(vc, v) and torch.equal(pc, pos)
     new_k = torch.randn(300, B, 1, H, D, generator=g, device=DEV).to(torch.bfloat16)
     for i in range(300):
-        cache.append(new_k[i], new_k[i] * 2, torch.full((1, 1), n + i, device=DEV))
+        cache.append(new_k[i], new_k[i] * 2, torch.full((B, 1), n + i, device=DEV))
     assert cache.capacity == int((n + 256) * 1.5)
     kc, vc, pc = cache.view()
     assert torch.equal(kc[:, :n], k) and torch.equal(kc[:, n:], new_k[:, :, 0].permute(1, 0, 2, 3))
     assert torch.equal(vc[:, n:], (new_k * 2)[:, :, 0].permute(1, 0, 2, 3))
-    assert torch.equal(pc[0], torch.arange(n + 300, device=DEV))
+    assert torch.equal(pc, torch.arange(n + 300, device=DEV).repeat(B, 1))
 
 
 def test_ring_decode_attention_single_rank():
@@ -149,3 +150,21 @@ def test_cached_ring_decode_multi_gpu(world, weights):
         assert held
         assert owners == res[0][1] and lengths == res[0][2]  # every rank reaches the same decisions
     assert sum(res[0][2]) == 1000 + steps
+
+
+@pytest.mark.parametrize("B,n", [(3, 1 << 19), (1, (1 << 20) + 8)])
+def test_append_split_over_launch_limit(B, n):
+    """Appends of 2^31 bytes or more per tensor are split over several launches (by sequence, then by token)."""
+    H, D = 8, 128
+    g = torch.Generator(device=DEV).manual_seed(n + B)
+    k = torch.randn(B, n, H, D, generator=g, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(B, n, H, D, generator=g, device=DEV, dtype=torch.bfloat16)
+    pos = torch.arange(n, device=DEV).repeat(B, 1)
+    cache = LayerKVCache(reserve=3)
+    cache.append(k[:, :-4], v[:, :-4], pos[:, :-4])  # split append from token-major sources
+    cache.append(k[:, -4:], v[:, -4:], pos[:, -4:])  # past the reserve: the grown buffer is filled by a split copy
+    assert cache.capacity == int((n - 4 + 3) * 1.5)
+    kc, vc, pc = cache.view()
+    assert torch.equal(kc, k) and torch.equal(vc, v) and torch.equal(pc, pos)
+    del kc, vc, pc, cache
+    torch.cuda.empty_cache()
