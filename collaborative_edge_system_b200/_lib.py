@@ -20,7 +20,7 @@ F32, F16, BF16, F64 = 0, 1, 2, 3
 _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
 
 CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE, CEA_ERR_NCCL = range(7)
-ABI_VERSION = 3
+ABI_VERSION = 4
 NCCL_ID_BYTES = 128
 MAX_PEERS = 16
 IPC_HANDLE_BYTES = 64
@@ -126,6 +126,21 @@ class CopyParams(ctypes.Structure):
     ]
 
 
+class WireCastParams(ctypes.Structure):
+    _fields_ = [
+        ("src", ctypes.c_void_p * 2),
+        ("dst", ctypes.c_void_p * 2),
+        ("src_stride", _i64x3 * 2),
+        ("dst_stride", _i64x3 * 2),
+        ("B", ctypes.c_int32),
+        ("S", ctypes.c_int32),
+        ("H", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("src_dtype", ctypes.c_int32),
+        ("dst_dtype", ctypes.c_int32),
+    ]
+
+
 class KvAppendParams(ctypes.Structure):
     _fields_ = [
         ("k", ctypes.c_void_p),
@@ -163,6 +178,7 @@ EXPORTS = (
     "cea_ulysses_pack",
     "cea_ulysses_unpack",
     "cea_kv_append",
+    "cea_wire_cast",
     "cea_device_status",
     "cea_last_error",
     "cea_abi_version",
@@ -206,6 +222,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             ("cea_ulysses_pack", [ctypes.POINTER(CopyParams), P], ctypes.c_int),
             ("cea_ulysses_unpack", [ctypes.POINTER(CopyParams), P], ctypes.c_int),
             ("cea_kv_append", [ctypes.POINTER(KvAppendParams), P], ctypes.c_int),
+            ("cea_wire_cast", [ctypes.POINTER(WireCastParams), P], ctypes.c_int),
             ("cea_device_status", [ctypes.POINTER(ctypes.c_int), ctypes.c_int, P], ctypes.c_int),
             ("cea_last_error", [], ctypes.c_char_p),
             ("cea_abi_version", [], ctypes.c_int),
@@ -419,6 +436,28 @@ def copy_segments(segments, D: int, elem_bytes: int, device: torch.device, entry
             s.dst_stride = _i64x3(dst.stride(0), dst.stride(1), dst.stride(2))
             s.nb, s.ns, s.nh = src.shape[0], src.shape[1], src.shape[2]
         _check(fn(ctypes.byref(p), _stream_ptr(device)), entry)
+
+
+def wire_cast(srcs: Sequence[torch.Tensor], dsts: Sequence[torch.Tensor]) -> None:
+    """cea_wire_cast: ``dsts[i] = srcs[i]`` converted to ``dsts[i].dtype`` for two ``[B, S, H, D]`` tensors
+    (any b/s/h strides, D contiguous), in one launch (float16 destinations saturate at +-65504)."""
+    if len(srcs) != 2 or len(dsts) != 2:
+        raise ValueError("wire_cast moves exactly two tensors (K and V)")
+    dev = require_cuda(*srcs, *dsts)
+    shape = tuple(srcs[0].shape)
+    for t in (*srcs, *dsts):
+        if t.dim() != 4 or tuple(t.shape) != shape or (t.numel() and t.stride(3) != 1):
+            raise ValueError("wire_cast needs four [B, S, H, D] tensors of one shape with a contiguous last dim")
+    if srcs[0].dtype != srcs[1].dtype or dsts[0].dtype != dsts[1].dtype:
+        raise ValueError("K and V must share their source dtype and their destination dtype")
+    p = WireCastParams()
+    for i in range(2):
+        p.src[i], p.dst[i] = srcs[i].data_ptr(), dsts[i].data_ptr()
+        p.src_stride[i] = _i64x3(*srcs[i].stride()[:3])
+        p.dst_stride[i] = _i64x3(*dsts[i].stride()[:3])
+    p.B, p.S, p.H, p.D = shape
+    p.src_dtype, p.dst_dtype = dtype_code(srcs[0].dtype), dtype_code(dsts[0].dtype)
+    _check(load().cea_wire_cast(ctypes.byref(p), _stream_ptr(dev)), "cea_wire_cast")
 
 
 def kv_append(k: torch.Tensor, v: torch.Tensor, pos: Optional[torch.Tensor], k_cache: torch.Tensor,

@@ -17,6 +17,7 @@
 #include "cea_nccl.cuh"
 #include "decode.cuh"
 #include "kv_cache.cuh"
+#include "wire.cuh"
 #include "peer_merge.cuh"
 
 using namespace cea;
@@ -687,6 +688,62 @@ static int copy_segments(const cea_copy_params* p, void* stream, const char* wha
 
 int cea_ulysses_pack(const cea_copy_params* p, void* stream) { return copy_segments(p, stream, "cea_ulysses_pack"); }
 int cea_ulysses_unpack(const cea_copy_params* p, void* stream) { return copy_segments(p, stream, "cea_ulysses_unpack"); }
+
+}  // extern "C"
+
+namespace {
+
+template <typename I>
+int launch_wire_to(const cea::wire::Args& a, int dst_dtype, dim3 grid, cudaStream_t s) {
+  switch (dst_dtype) {
+    case CEA_F32: cea::wire::wire_cast_kernel<I, float><<<grid, cea::wire::kThreads, 0, s>>>(a); return CEA_OK;
+    case CEA_F16: cea::wire::wire_cast_kernel<I, __half><<<grid, cea::wire::kThreads, 0, s>>>(a); return CEA_OK;
+    case CEA_BF16: cea::wire::wire_cast_kernel<I, __nv_bfloat16><<<grid, cea::wire::kThreads, 0, s>>>(a); return CEA_OK;
+    case CEA_F64: cea::wire::wire_cast_kernel<I, double><<<grid, cea::wire::kThreads, 0, s>>>(a); return CEA_OK;
+  }
+  return fail(CEA_ERR_UNSUPPORTED, "cea_wire_cast: destination dtype %d", dst_dtype);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cea_wire_cast(const cea_wire_cast_params* p, void* stream) {
+  const char* what = "cea_wire_cast";
+  if (p == nullptr) return fail(CEA_ERR_INVALID, "%s: null params", what);
+  if (p->B < 0 || p->S < 0 || p->H < 0 || p->D < 0) return fail(CEA_ERR_INVALID, "%s: negative size", what);
+  const auto known = [](int d) { return d == CEA_F32 || d == CEA_F16 || d == CEA_BF16 || d == CEA_F64; };
+  if (!known(p->src_dtype) || !known(p->dst_dtype)) return fail(CEA_ERR_UNSUPPORTED, "%s: dtype", what);
+  const int64_t elems = static_cast<int64_t>(p->B) * p->S * p->H * p->D;
+  if (elems == 0) return CEA_OK;
+  for (int t = 0; t < 2; ++t)
+    if (p->src[t] == nullptr || p->dst[t] == nullptr) return fail(CEA_ERR_INVALID, "%s: null tensor %d", what, t);
+  cea::wire::Args a{};
+  for (int t = 0; t < 2; ++t) {
+    a.src[t] = p->src[t];
+    a.dst[t] = p->dst[t];
+    for (int j = 0; j < 3; ++j) {
+      a.src_stride[t][j] = p->src_stride[t][j];
+      a.dst_stride[t][j] = p->dst_stride[t][j];
+    }
+  }
+  a.B = p->B;
+  a.S = p->S;
+  a.H = p->H;
+  a.D = p->D;
+  const int64_t groups = elems / p->D * ((p->D + cea::wire::kVec - 1) / cea::wire::kVec);
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>((groups + cea::wire::kThreads - 1) / cea::wire::kThreads,
+                                                          148 * 8)), 2);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc = CEA_OK;
+  switch (p->src_dtype) {
+    case CEA_F32: rc = launch_wire_to<float>(a, p->dst_dtype, grid, s); break;
+    case CEA_F16: rc = launch_wire_to<__half>(a, p->dst_dtype, grid, s); break;
+    case CEA_BF16: rc = launch_wire_to<__nv_bfloat16>(a, p->dst_dtype, grid, s); break;
+    default: rc = launch_wire_to<double>(a, p->dst_dtype, grid, s); break;
+  }
+  return rc != CEA_OK ? rc : cuda_check(what);
+}
 
 int cea_kv_append(const cea_kv_append_params* p, void* stream) {
   const char* what = "cea_kv_append";

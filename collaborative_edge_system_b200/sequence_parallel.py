@@ -95,8 +95,9 @@ def ring_attention(
     acc = accumulation_dtype(q.dtype)
     out = torch.empty(B, Sq, Hq, D, dtype=acc, device=q.device)
     lse = torch.empty(B, Hq, Sq, dtype=acc, device=q.device)
-    # K and V travel as one message (optionally narrower); received blocks are forwarded as they arrive
-    wire = comm.to_wire(torch.stack([k, v])).contiguous()
+    # K and V travel as one message in the communicator's wire dtype (narrower when it compresses), packed and
+    # converted by one kernel; received blocks are forwarded as they arrived, widened only for the attention
+    wire = _pack_wire(k, v, comm.wire_dtype(k.dtype))
     k_cur, v_cur = k, v
     pos = k_pos.to(device=q.device, dtype=torch.int64).contiguous()
     nxt, prv = (r + 1) % n, (r - 1) % n
@@ -111,9 +112,28 @@ def ring_attention(
                     accumulate=step > 0)
         if pending is not None:
             wire, pos = pending.wait()
-            k_cur, v_cur = wire[0].to(k.dtype), wire[1].to(k.dtype)
+            k_cur, v_cur = _unpack_wire(wire, k.dtype)
     res = out.to(q.dtype)
     return (res, lse) if return_lse else res
+
+
+def _pack_wire(k: torch.Tensor, v: torch.Tensor, wire_dtype: torch.dtype) -> torch.Tensor:
+    """The ``[2, B, s, Hkv, D]`` K||V message of a ring step in ``wire_dtype`` (``sequence_parallel.py:101-103``):
+    one ``cea_wire_cast`` launch does the stack and the conversion (float16 saturating as ``to_wire`` does)."""
+    wire = torch.empty((2,) + tuple(k.shape), dtype=wire_dtype, device=k.device)
+    _lib.wire_cast((k if k.stride(3) == 1 else k.contiguous(), v if v.stride(3) == 1 else v.contiguous()),
+                   (wire[0], wire[1]))
+    return wire
+
+
+def _unpack_wire(wire: torch.Tensor, dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    """K and V of a received message in the compute dtype (``sequence_parallel.py:129``); views when no
+    conversion is needed, else one ``cea_wire_cast`` launch."""
+    if wire.dtype == dtype:
+        return wire[0], wire[1]
+    out = torch.empty(wire.shape, dtype=dtype, device=wire.device)
+    _lib.wire_cast((wire[0], wire[1]), (out[0], out[1]))
+    return out[0], out[1]
 
 
 # ----------------------------------------------------------------------------

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define CEA_ABI_VERSION 3
+#define CEA_ABI_VERSION 4
 
 enum cea_status {
   CEA_OK = 0,
@@ -182,6 +182,28 @@ typedef struct cea_copy_params {
 
 int cea_ulysses_pack(const cea_copy_params* p, void* stream);
 int cea_ulysses_unpack(const cea_copy_params* p, void* stream);
+
+/*
+ * Ring wire pack / unpack (collab_infer parallel/sequence_parallel.py:101-103
+ * and :129, over Communicator.to_wire, distributed/comm.py:275-290): two
+ * [B, S, H, D] tensors (K and V; element strides b, s, h per tensor, D
+ * contiguous) copied into two destinations with a dtype conversion in the
+ * same pass.  Packing writes the K||V message of a ring step in the wire
+ * dtype; unpacking widens a received message back to the compute dtype.
+ * Conversions follow torch: float64 goes through float32, narrowing rounds
+ * to nearest even, and a float16 destination saturates at +-65504 (NaN is
+ * kept) unless the source is float16 too.
+ */
+typedef struct cea_wire_cast_params {
+  const void* src[2];
+  void* dst[2];
+  int64_t src_stride[2][3];
+  int64_t dst_stride[2][3];
+  int32_t B, S, H, D;
+  int32_t src_dtype, dst_dtype; /* cea_dtype */
+} cea_wire_cast_params;
+
+int cea_wire_cast(const cea_wire_cast_params* p, void* stream);
 
 /*
  * KV-cache append (collab_infer models/cache.py:51-62, LayerKVCache.append):

@@ -150,6 +150,36 @@ def merge_attention_list(outs: Sequence[np.ndarray], lses: Sequence[np.ndarray])
     return out, lse
 
 
+def to_bfloat16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> bfloat16 bit patterns (uint16), round to nearest, ties to even; NaN stays NaN."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rounded = (u + (np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1)))) >> 16
+    nan = np.isnan(x)
+    return np.where(nan, (u >> 16) | np.uint32(0x40), rounded).astype(np.uint16)
+
+
+def from_bfloat16_bits(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def to_wire(x: np.ndarray, wire: Optional[str]) -> np.ndarray:
+    """A tensor as received through a wire of dtype ``wire`` (``distributed/comm.py:275-290``), back in
+    its own dtype: the cast happens only when the wire type is narrower, and float16 saturates at
+    +-65504 instead of overflowing."""
+    if wire is None:
+        return x
+    wire = {"int8": "bfloat16"}.get(wire, wire)  # comm.py:54: int8 compression sends activations as bfloat16
+    itemsize = {"float16": 2, "bfloat16": 2, "float32": 4, "float64": 8}[wire]
+    if itemsize >= x.dtype.itemsize:
+        return x
+    if wire == "float32":
+        return x.astype(np.float32).astype(x.dtype)
+    # a float64 input is rounded to float32 first, as torch's conversion does
+    if wire == "float16":
+        return np.clip(x, -65504.0, 65504.0).astype(np.float32).astype(np.float16).astype(x.dtype)
+    return from_bfloat16_bits(to_bfloat16_bits(x.astype(np.float32))).astype(x.dtype)
+
+
 def ring_attention(
     q_shards: List[np.ndarray],
     k_shards: List[np.ndarray],
@@ -159,13 +189,17 @@ def ring_attention(
     scale: Optional[float] = None,
     kv_map=None,
     acc=np.float64,
+    wire: Optional[str] = None,
 ) -> List[Tuple[np.ndarray, np.ndarray]]:
     """All ranks of ``parallel/sequence_parallel.py:68-130`` simulated in one process.
 
     Rank r meets the block of rank ``(r - t) % n`` at step t, skips fully
-    masked blocks and merges pairwise in that order.  Returns ``(out, lse)``
-    per rank in ``acc`` precision (the reference drops the LSE at ``:130``;
-    it is kept here because the product offers it with ``return_lse=True``).
+    masked blocks and merges pairwise in that order.  With a ``wire`` dtype
+    (``comm_dtype``, ``:101-103,129``) every received block is the
+    wire-rounded one while the rank's own block stays exact.  Returns
+    ``(out, lse)`` per rank in ``acc`` precision (the reference drops the LSE
+    at ``:130``; it is kept here because the product offers it with
+    ``return_lse=True``).
     """
     n = len(q_shards)
     results = []
@@ -177,7 +211,10 @@ def ring_attention(
             kp = pos_shards[src]
             if fully_masked(qp, kp, causal):
                 continue
-            o, l = attention_with_lse(q, k_shards[src], v_shards[src], qp, kp, causal, scale, kv_map, acc)
+            k, v = k_shards[src], v_shards[src]
+            if step > 0:
+                k, v = to_wire(k, wire), to_wire(v, wire)
+            o, l = attention_with_lse(q, k, v, qp, kp, causal, scale, kv_map, acc)
             out, lse = (o, l) if out is None else merge_attention(out, lse, o, l)
         if out is None:
             B, Sq, Hq, D = q.shape

@@ -46,3 +46,8 @@ def golden_cache_engine():
 
     with open(os.path.join(GOLDEN, "kv_cache_engine.json")) as f:
         return json.load(f)
+
+
+@pytest.fixture(scope="session")
+def golden_wire():
+    return load_golden("ring_wire.npz")

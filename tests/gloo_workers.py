@@ -64,6 +64,17 @@ def install_oracle_compute():
 
     cache_mod._copy_tokens = copy_tokens
     cache_mod._check_device = lambda *tensors: None
+    def pack_wire(k, v, wire_dtype):
+        kv = torch.stack([k, v])
+        if wire_dtype != kv.dtype:
+            kv = (kv.clamp(-65504.0, 65504.0) if wire_dtype == torch.float16 else kv).to(wire_dtype)
+        return kv
+
+    def unpack_wire(wire, dtype):
+        return wire[0].to(dtype), wire[1].to(dtype)
+
+    sp._pack_wire = pack_wire
+    sp._unpack_wire = unpack_wire
     sp.attend_into = attend_into
     sp.attention_with_lse = attention_with_lse
     sp.attention = attention
@@ -102,6 +113,21 @@ def cached_decode_worker(rank, world, weights, prompt, steps):
                                pos_all[:, sl].numpy(), pos_all[:, : t + 1].numpy(), True)
         errs.append(float(np.abs(out.numpy() - ref).max()))
     return max(errs), owners, kv.sp_lengths, len(layer), layer.capacity
+
+
+def wire_ring_worker(rank, world, case):
+    """The product's ring over gloo with a compressed wire (``comm_dtype``), compute by the oracle."""
+    install_oracle_compute()
+    from collaborative_edge_system_b200 import ParallelContext, SequenceLayout
+    from collaborative_edge_system_b200.sequence_parallel import ring_attention
+
+    m = meta(case)
+    ctx = ParallelContext(1, world, 1, comm_dtype=m["comm_dtype"])
+    q, k, v, pos = (torch.from_numpy(case[key]) for key in ("q", "k", "v", "pos"))
+    layout = SequenceLayout(q.shape[1], world, m["weights"], m["kind"])
+    ql, kl, vl, pl = (layout.shard(t, rank) for t in (q, k, v, pos))
+    out = ring_attention(ql, kl, vl, pl, pl, ctx.sp, layout.sizes, causal=True)
+    return out.numpy(), ctx.stats.total_bytes
 
 
 def golden_inputs():

@@ -207,3 +207,19 @@ def cached_decode_worker(rank, world, prompt, steps, B, Hq, Hkv, D, weights):
     held = (torch.equal(kc.cpu(), k_all[:, mine]) and torch.equal(vc.cpu(), v_all[:, mine])
             and torch.equal(pc.cpu(), pos_all[:, mine]))
     return max(errs), owners, kv.sp_lengths, held
+
+
+def wire_ring_worker(rank, world, case):
+    """Ring attention on NCCL with a compressed wire (``comm_dtype``) on the reference's golden inputs."""
+    import json
+
+    import collaborative_edge_system_b200 as cea
+
+    m = json.loads(str(case["meta"]))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev, comm_dtype=m["comm_dtype"])
+    q, k, v, pos = (torch.from_numpy(case[key]) for key in ("q", "k", "v", "pos"))
+    lay = cea.SequenceLayout(q.shape[1], world, m["weights"], m["kind"])
+    ql, kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (q, k, v, pos))
+    out = cea.ring_attention(ql, kl, vl, pl, pl, ctx.sp, lay.sizes, causal=True)
+    return out.cpu().numpy(), ctx.stats.total_bytes

@@ -29,7 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.cea_abi_version() == _lib.ABI_VERSION == 3
+    assert lib.cea_abi_version() == _lib.ABI_VERSION == 4
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
@@ -91,6 +91,21 @@ def test_kv_append_rejects_bad_arguments_without_a_gpu():
     assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_OK
 
 
+def test_wire_cast_rejects_bad_arguments_without_a_gpu():
+    lib = _lib.load()
+    assert lib.cea_wire_cast(None, None) == _lib.CEA_ERR_INVALID
+    wp = _lib.WireCastParams()
+    wp.B, wp.S, wp.H, wp.D = 1, 4, 2, 8
+    wp.src_dtype, wp.dst_dtype = _lib.F32, 7
+    assert lib.cea_wire_cast(ctypes.byref(wp), None) == _lib.CEA_ERR_UNSUPPORTED
+    wp.dst_dtype = _lib.BF16
+    assert lib.cea_wire_cast(ctypes.byref(wp), None) == _lib.CEA_ERR_INVALID  # null tensors
+    wp.S = -1
+    assert lib.cea_wire_cast(ctypes.byref(wp), None) == _lib.CEA_ERR_INVALID
+    wp.S = 0  # nothing to convert: no launch
+    assert lib.cea_wire_cast(ctypes.byref(wp), None) == _lib.CEA_OK
+
+
 def test_product_path_refuses_cpu_tensors():
     import torch
 
@@ -124,6 +139,9 @@ int main(void) {
   P(cea_kv_append_params, kc_stride); P(cea_kv_append_params, pos); P(cea_kv_append_params, pc_stride);
   P(cea_kv_append_params, B); P(cea_kv_append_params, v_elem_bytes); P(cea_kv_append_params, offset);
   P(cea_kv_append_params, capacity);
+  printf("cea_wire_cast_params %zu\n", sizeof(cea_wire_cast_params));
+  P(cea_wire_cast_params, dst); P(cea_wire_cast_params, src_stride); P(cea_wire_cast_params, dst_stride);
+  P(cea_wire_cast_params, B); P(cea_wire_cast_params, dst_dtype);
   return 0;
 }
 """
@@ -146,10 +164,12 @@ def test_struct_layout_matches_ctypes():
     assert c["cea_copy_params"] == ctypes.sizeof(_lib.CopyParams)
     assert c["cea_peer_merge_params"] == ctypes.sizeof(_lib.PeerMergeParams)
     assert c["cea_kv_append_params"] == ctypes.sizeof(_lib.KvAppendParams)
+    assert c["cea_wire_cast_params"] == ctypes.sizeof(_lib.WireCastParams)
     for key, val in c.items():
         if "." in key:
             struct, field = key.split(".")
             cls = {"cea_attn_params": _lib.AttnParams, "cea_merge_params": _lib.MergeParams,
                    "cea_segment": _lib.Segment, "cea_copy_params": _lib.CopyParams,
-                   "cea_peer_merge_params": _lib.PeerMergeParams, "cea_kv_append_params": _lib.KvAppendParams}[struct]
+                   "cea_peer_merge_params": _lib.PeerMergeParams, "cea_kv_append_params": _lib.KvAppendParams,
+                   "cea_wire_cast_params": _lib.WireCastParams}[struct]
             assert getattr(cls, field).offset == val, key

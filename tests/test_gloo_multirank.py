@@ -91,3 +91,19 @@ def test_cached_ring_decode_host_flow(world, weights):
         assert held == lengths[r] == lay.sizes[r] + owners.count(r)
         assert cap >= held
     assert sum(res[0][2]) == prompt + steps
+
+
+WIRE_CASES = ["w2_bf16_f32", "w3_f16_f32_zigzag_sat", "w2_bf16_f64", "w2_f16_f32_gqa"]
+
+
+@pytest.mark.parametrize("name", WIRE_CASES)
+def test_ring_with_compressed_wire_matches_reference(golden_wire, name):
+    """Ring attention with ``comm_dtype``: remote K/V blocks arrive wire-rounded (float16 saturating), the
+    local block stays exact, and the bytes sent equal the reference's."""
+    case = golden_wire[name]
+    m = W.meta(case)
+    for r, (out, sent) in enumerate(_run(W.wire_ring_worker, m["world"], case)):
+        want = case[f"r{r}/out"]
+        tol = (1e-12 if m["dtype"] == "float64" else 2e-6) * max(1.0, float(np.abs(want).max()))
+        assert np.abs(out - want).max() <= tol, (r, np.abs(out - want).max())
+        assert sent == int(case[f"r{r}/bytes"])

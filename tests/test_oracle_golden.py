@@ -139,3 +139,21 @@ def test_ulysses_chunked_fp64(golden_sp):
     valid = pos >= 0
     for r in range(3):
         _close(golden_sp["ulysses_chunked"][f"r{r}/full"][valid], full[valid], TOL64)
+
+
+@pytest.mark.parametrize("name", ["w2_bf16_f32", "w3_f16_f32_zigzag_sat", "w2_bf16_f64", "w2_f16_f32_gqa"])
+def test_oracle_ring_with_compressed_wire(golden_wire, name):
+    """The oracle's ring with a wire dtype reproduces the reference's ring under ``comm_dtype``."""
+    c = golden_wire[name]
+    m = json.loads(str(c["meta"]))
+    lay = SequenceLayout(c["q"].shape[1], m["world"], m["weights"], m["kind"])
+    sh = [[c[key][:, lay.indices(r).numpy()] for r in range(m["world"])] for key in ("q", "k", "v", "pos")]
+    res = oracle.ring_attention(*sh, causal=True, wire=m["comm_dtype"])
+    plain = oracle.ring_attention(*sh, causal=True)
+    for r, (o, _) in enumerate(res):
+        want = c[f"r{r}/out"]
+        scale = max(1.0, float(np.abs(want).max()))
+        tol = (1e-12 if m["dtype"] == "float64" else 2e-6) * scale
+        assert np.abs(o - want).max() <= tol, (r, np.abs(o - want).max())
+    # the rounding is visible: without it some rank's result moves far past the tolerance
+    assert any(np.abs(p[0] - w[0]).max() > 1e-4 * max(1.0, float(np.abs(w[0]).max())) for p, w in zip(plain, res))
