@@ -20,7 +20,7 @@ F32, F16, BF16, F64 = 0, 1, 2, 3
 _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
 
 CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE, CEA_ERR_NCCL = range(7)
-ABI_VERSION = 4
+ABI_VERSION = 5
 NCCL_ID_BYTES = 128
 MAX_PEERS = 16
 IPC_HANDLE_BYTES = 64
@@ -141,6 +141,53 @@ class WireCastParams(ctypes.Structure):
     ]
 
 
+class RmsNormParams(ctypes.Structure):
+    _fields_ = [
+        ("resid", ctypes.c_void_p),
+        ("delta", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("h", ctypes.c_int64),
+        ("resid_stride", ctypes.c_int64),
+        ("delta_stride", ctypes.c_int64),
+        ("y_stride", ctypes.c_int64),
+        ("eps", ctypes.c_double),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+class RopeParams(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("q_stride", _i64x3),
+        ("k_stride", _i64x3),
+        ("pos", ctypes.c_void_p),
+        ("pos_stride", _i64x2),
+        ("inv_freq", ctypes.c_void_p),
+        ("B", ctypes.c_int32),
+        ("S", ctypes.c_int32),
+        ("Hq", ctypes.c_int32),
+        ("Hk", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+class SiluMulParams(ctypes.Structure):
+    _fields_ = [
+        ("gate", ctypes.c_void_p),
+        ("up", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("n", ctypes.c_int64),
+        ("in_stride", ctypes.c_int64),
+        ("out_stride", ctypes.c_int64),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
 class KvAppendParams(ctypes.Structure):
     _fields_ = [
         ("k", ctypes.c_void_p),
@@ -179,6 +226,9 @@ EXPORTS = (
     "cea_ulysses_unpack",
     "cea_kv_append",
     "cea_wire_cast",
+    "cea_add_rmsnorm",
+    "cea_rope",
+    "cea_silu_mul",
     "cea_device_status",
     "cea_last_error",
     "cea_abi_version",
@@ -223,6 +273,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             ("cea_ulysses_unpack", [ctypes.POINTER(CopyParams), P], ctypes.c_int),
             ("cea_kv_append", [ctypes.POINTER(KvAppendParams), P], ctypes.c_int),
             ("cea_wire_cast", [ctypes.POINTER(WireCastParams), P], ctypes.c_int),
+            ("cea_add_rmsnorm", [ctypes.POINTER(RmsNormParams), P], ctypes.c_int),
+            ("cea_rope", [ctypes.POINTER(RopeParams), P], ctypes.c_int),
+            ("cea_silu_mul", [ctypes.POINTER(SiluMulParams), P], ctypes.c_int),
             ("cea_device_status", [ctypes.POINTER(ctypes.c_int), ctypes.c_int, P], ctypes.c_int),
             ("cea_last_error", [], ctypes.c_char_p),
             ("cea_abi_version", [], ctypes.c_int),
@@ -458,6 +511,79 @@ def wire_cast(srcs: Sequence[torch.Tensor], dsts: Sequence[torch.Tensor]) -> Non
     p.B, p.S, p.H, p.D = shape
     p.src_dtype, p.dst_dtype = dtype_code(srcs[0].dtype), dtype_code(dsts[0].dtype)
     _check(load().cea_wire_cast(ctypes.byref(p), _stream_ptr(dev)), "cea_wire_cast")
+
+
+def _rows(t: torch.Tensor, h: int) -> int:
+    """Elements between consecutive rows of a tensor viewed as ``[rows, h]`` (last dim contiguous)."""
+    if t.stride(-1) != 1 or t.shape[-1] != h:
+        raise ValueError("rows must be contiguous in their last dimension")
+    if t.dim() == 1:
+        return h
+    # every leading dimension must step by whole rows of the same pitch
+    pitch = t.stride(-2)
+    expect = pitch
+    for d in range(t.dim() - 2, -1, -1):
+        if t.shape[d] > 1 and t.stride(d) != expect:
+            raise ValueError("leading dimensions must be uniformly strided rows")
+        expect *= t.shape[d]
+    return pitch
+
+
+def add_rmsnorm(resid: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Tensor, y: torch.Tensor,
+                eps: float) -> None:
+    """cea_add_rmsnorm: ``resid += delta`` (if given), then ``y = rmsnorm(resid) * weight``, over the last dim."""
+    dev = require_cuda(resid, delta, weight, y)
+    h = resid.shape[-1]
+    dts = {resid.dtype, weight.dtype, y.dtype} | ({delta.dtype} if delta is not None else set())
+    if len(dts) != 1:
+        raise ValueError("residual, delta, weight and output must share a dtype")
+    if weight.shape != (h,) or y.shape != resid.shape or (delta is not None and delta.shape != resid.shape):
+        raise ValueError("add_rmsnorm shapes disagree")
+    p = RmsNormParams()
+    p.resid, p.weight, p.y = resid.data_ptr(), weight.data_ptr(), y.data_ptr()
+    p.rows, p.h = resid.numel() // max(h, 1), h
+    p.resid_stride, p.y_stride = _rows(resid, h), _rows(y, h)
+    if delta is not None:
+        p.delta, p.delta_stride = delta.data_ptr(), _rows(delta, h)
+    p.eps, p.dtype = float(eps), dtype_code(resid.dtype)
+    _check(load().cea_add_rmsnorm(ctypes.byref(p), _stream_ptr(dev)), "cea_add_rmsnorm")
+
+
+def rope(q: torch.Tensor, k: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> None:
+    """cea_rope: rotary embedding of ``q`` ``[B, S, Hq, D]`` and ``k`` ``[B, S, Hk, D]`` in place."""
+    dev = require_cuda(q, k, pos, inv_freq)
+    B, S, Hq, D = q.shape
+    if k.shape[:2] != (B, S) or k.shape[3] != D or q.dtype != k.dtype or q.stride(3) != 1 or k.stride(3) != 1:
+        raise ValueError("q and k must be [B, S, H, D] of one dtype with a contiguous last dimension")
+    want = torch.float64 if q.dtype == torch.float64 else torch.float32
+    if inv_freq.dtype != want or inv_freq.numel() != D // 2 or not inv_freq.is_contiguous():
+        raise ValueError(f"inv_freq must be {D // 2} contiguous {want} values")
+    if pos.dtype != torch.int64 or tuple(pos.shape) != (B, S):
+        raise ValueError("positions must be [B, S] int64")
+    p = RopeParams()
+    p.q, p.k = q.data_ptr(), k.data_ptr()
+    p.q_stride, p.k_stride = _i64x3(*q.stride()[:3]), _i64x3(*k.stride()[:3])
+    p.pos, p.pos_stride = pos.data_ptr(), _i64x2(*pos.stride())
+    p.inv_freq = inv_freq.data_ptr()
+    p.B, p.S, p.Hq, p.Hk, p.D = B, S, Hq, k.shape[2], D
+    p.dtype = dtype_code(q.dtype)
+    _check(load().cea_rope(ctypes.byref(p), _stream_ptr(dev)), "cea_rope")
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> None:
+    """cea_silu_mul: ``out = silu(gate) * up`` (gate and up: row views of one fused projection)."""
+    dev = require_cuda(gate, up, out)
+    n = gate.shape[-1]
+    if up.shape != gate.shape or out.shape != gate.shape or len({gate.dtype, up.dtype, out.dtype}) != 1:
+        raise ValueError("gate, up and out must share shape and dtype")
+    if _rows(gate, n) != _rows(up, n):
+        raise ValueError("gate and up must have the same row pitch")
+    p = SiluMulParams()
+    p.gate, p.up, p.out = gate.data_ptr(), up.data_ptr(), out.data_ptr()
+    p.rows, p.n = gate.numel() // max(n, 1), n
+    p.in_stride, p.out_stride = _rows(gate, n), _rows(out, n)
+    p.dtype = dtype_code(gate.dtype)
+    _check(load().cea_silu_mul(ctypes.byref(p), _stream_ptr(dev)), "cea_silu_mul")
 
 
 def kv_append(k: torch.Tensor, v: torch.Tensor, pos: Optional[torch.Tensor], k_cache: torch.Tensor,

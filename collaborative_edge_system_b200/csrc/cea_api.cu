@@ -18,6 +18,7 @@
 #include "decode.cuh"
 #include "kv_cache.cuh"
 #include "wire.cuh"
+#include "llama_ops.cuh"
 #include "peer_merge.cuh"
 
 using namespace cea;
@@ -743,6 +744,84 @@ int cea_wire_cast(const cea_wire_cast_params* p, void* stream) {
     default: rc = launch_wire_to<double>(a, p->dst_dtype, grid, s); break;
   }
   return rc != CEA_OK ? rc : cuda_check(what);
+}
+
+int cea_add_rmsnorm(const cea_rmsnorm_params* p, void* stream) {
+  const char* what = "cea_add_rmsnorm";
+  if (p == nullptr) return fail(CEA_ERR_INVALID, "%s: null params", what);
+  if (p->rows < 0 || p->h < 1) return fail(CEA_ERR_INVALID, "%s: rows >= 0 and h >= 1", what);
+  if (p->rows == 0) return CEA_OK;
+  if (!p->resid || !p->weight || !p->y) return fail(CEA_ERR_INVALID, "%s: null pointer", what);
+  if (!(p->eps >= 0.0)) return fail(CEA_ERR_INVALID, "%s: eps", what);
+  cea::llama::NormArgs a{p->resid, p->delta, p->weight, p->y, p->rows, p->h,
+                         p->resid_stride, p->delta_stride, p->y_stride, p->eps};
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(p->rows, 148 * 16));
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (p->dtype) {
+    case CEA_F32: cea::llama::add_rmsnorm_kernel<float><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
+    case CEA_F16: cea::llama::add_rmsnorm_kernel<__half><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
+    case CEA_BF16: cea::llama::add_rmsnorm_kernel<__nv_bfloat16><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
+    case CEA_F64: cea::llama::add_rmsnorm_kernel<double><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
+    default: return fail(CEA_ERR_UNSUPPORTED, "%s: dtype %d", what, p->dtype);
+  }
+  return cuda_check(what);
+}
+
+int cea_rope(const cea_rope_params* p, void* stream) {
+  const char* what = "cea_rope";
+  if (p == nullptr) return fail(CEA_ERR_INVALID, "%s: null params", what);
+  if (p->B < 0 || p->S < 0 || p->Hq < 0 || p->Hk < 0 || p->D < 2 || (p->D & 1))
+    return fail(CEA_ERR_INVALID, "%s: sizes (D even and >= 2)", what);
+  const int64_t most = static_cast<int64_t>(p->B) * p->S * std::max(p->Hq, p->Hk) * (p->D / 2);
+  if (most == 0) return CEA_OK;
+  if (!p->pos || !p->inv_freq || (p->Hq && !p->q) || (p->Hk && !p->k)) return fail(CEA_ERR_INVALID, "%s: null pointer", what);
+  cea::llama::RopeArgs a{};
+  a.x[0] = p->q;
+  a.x[1] = p->k;
+  for (int j = 0; j < 3; ++j) {
+    a.stride[0][j] = p->q_stride[j];
+    a.stride[1][j] = p->k_stride[j];
+  }
+  a.H[0] = p->Hq;
+  a.H[1] = p->Hk;
+  a.pos = p->pos;
+  a.pos_stride[0] = p->pos_stride[0];
+  a.pos_stride[1] = p->pos_stride[1];
+  a.inv_freq = p->inv_freq;
+  a.B = p->B;
+  a.S = p->S;
+  a.D = p->D;
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>((most + cea::llama::kEltThreads - 1) / cea::llama::kEltThreads,
+                                                          148 * 8)), 2);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (p->dtype) {
+    case CEA_F32: cea::llama::rope_kernel<float><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F16: cea::llama::rope_kernel<__half><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_BF16: cea::llama::rope_kernel<__nv_bfloat16><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F64: cea::llama::rope_kernel<double><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    default: return fail(CEA_ERR_UNSUPPORTED, "%s: dtype %d", what, p->dtype);
+  }
+  return cuda_check(what);
+}
+
+int cea_silu_mul(const cea_silu_mul_params* p, void* stream) {
+  const char* what = "cea_silu_mul";
+  if (p == nullptr) return fail(CEA_ERR_INVALID, "%s: null params", what);
+  if (p->rows < 0 || p->n < 0) return fail(CEA_ERR_INVALID, "%s: sizes", what);
+  if (p->rows * p->n == 0) return CEA_OK;
+  if (!p->gate || !p->up || !p->out) return fail(CEA_ERR_INVALID, "%s: null pointer", what);
+  cea::llama::SiluArgs a{p->gate, p->up, p->out, p->rows, p->n, p->in_stride, p->out_stride};
+  const unsigned grid = static_cast<unsigned>(
+      std::min<int64_t>((p->rows * p->n + cea::llama::kEltThreads - 1) / cea::llama::kEltThreads, 148 * 8));
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (p->dtype) {
+    case CEA_F32: cea::llama::silu_mul_kernel<float><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F16: cea::llama::silu_mul_kernel<__half><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_BF16: cea::llama::silu_mul_kernel<__nv_bfloat16><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F64: cea::llama::silu_mul_kernel<double><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    default: return fail(CEA_ERR_UNSUPPORTED, "%s: dtype %d", what, p->dtype);
+  }
+  return cuda_check(what);
 }
 
 int cea_kv_append(const cea_kv_append_params* p, void* stream) {

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define CEA_ABI_VERSION 4
+#define CEA_ABI_VERSION 5
 
 enum cea_status {
   CEA_OK = 0,
@@ -204,6 +204,68 @@ typedef struct cea_wire_cast_params {
 } cea_wire_cast_params;
 
 int cea_wire_cast(const cea_wire_cast_params* p, void* stream);
+
+/*
+ * The decoder-layer steps around the attention for a LLaMA-family prefill
+ * or decode on the sequence-parallel path (collab_infer models/llama.py).
+ * Values are rounded to the model dtype wherever the reference's tensor
+ * expressions round them.
+ *
+ * cea_add_rmsnorm: resid <- resid + delta (if delta != NULL), then
+ *   y = w * (resid * rsqrt(mean(resid^2) + eps)) over the last dimension h,
+ *   the normalisation in fp32 (fp64 for an fp64 model); RMSNorm.forward,
+ *   llama.py:52-61, fused with the residual adds of DecoderLayer.forward,
+ *   :337-339.  Rows are contiguous; strides count elements between rows.
+ */
+typedef struct cea_rmsnorm_params {
+  void* resid;
+  const void* delta;
+  const void* weight;
+  void* y;
+  int64_t rows, h;
+  int64_t resid_stride, delta_stride, y_stride;
+  double eps;
+  int32_t dtype;
+} cea_rmsnorm_params;
+
+int cea_add_rmsnorm(const cea_rmsnorm_params* p, void* stream);
+
+/*
+ * cea_rope: in place, x <- x * cos + rotate_half(x) * sin for q
+ * [B, S, Hq, D] and k [B, S, Hk, D] (element strides b, s, h; D contiguous)
+ * with cos / sin of max(pos, 0) * inv_freq (RotaryEmbedding and
+ * apply_rotary, llama.py:64-88).  inv_freq holds D/2 floats (doubles for an
+ * fp64 model); pos is [B, S] int64.
+ */
+typedef struct cea_rope_params {
+  void* q;
+  void* k;
+  int64_t q_stride[3];
+  int64_t k_stride[3];
+  const int64_t* pos;
+  int64_t pos_stride[2];
+  const void* inv_freq;
+  int32_t B, S, Hq, Hk, D;
+  int32_t dtype;
+} cea_rope_params;
+
+int cea_rope(const cea_rope_params* p, void* stream);
+
+/*
+ * cea_silu_mul: out = silu(gate) * up for rows of n units (ParallelMLP,
+ * llama.py:301-305); gate and up rows are in_stride elements apart (the two
+ * halves of the fused gate/up projection).
+ */
+typedef struct cea_silu_mul_params {
+  const void* gate;
+  const void* up;
+  void* out;
+  int64_t rows, n;
+  int64_t in_stride, out_stride;
+  int32_t dtype;
+} cea_silu_mul_params;
+
+int cea_silu_mul(const cea_silu_mul_params* p, void* stream);
 
 /*
  * KV-cache append (collab_infer models/cache.py:51-62, LayerKVCache.append):

@@ -25,3 +25,4 @@ from .attention_ref import (  # noqa: F401
     visibility,
 )
 from . import kv_cache  # noqa: F401,E402
+from . import llama_ref  # noqa: F401,E402

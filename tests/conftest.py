@@ -51,3 +51,9 @@ def golden_cache_engine():
 @pytest.fixture(scope="session")
 def golden_wire():
     return load_golden("ring_wire.npz")
+
+
+@pytest.fixture(scope="session")
+def golden_llama():
+    data = np.load(os.path.join(GOLDEN, "llama_sp.npz"), allow_pickle=False)
+    return {k: data[k] for k in data.files}

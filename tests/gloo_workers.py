@@ -73,6 +73,25 @@ def install_oracle_compute():
     def unpack_wire(wire, dtype):
         return wire[0].to(dtype), wire[1].to(dtype)
 
+    import collaborative_edge_system_b200.llama as llama_mod
+    from collaborative_edge_system_b200 import _lib
+
+    def add_rmsnorm(resid, delta, weight, y, eps):
+        if delta is not None:
+            resid.add_(delta)
+        y.copy_(torch.from_numpy(oracle.llama_ref.rms_norm(npy(resid), npy(weight), eps)))
+
+    def rope(q, k, pos, inv_freq):
+        cos, sin = oracle.llama_ref.rotary_cos_sin(npy(pos), npy(inv_freq), npy(q).dtype)
+        q.copy_(torch.from_numpy(oracle.llama_ref.apply_rotary(npy(q), cos, sin)))
+        k.copy_(torch.from_numpy(oracle.llama_ref.apply_rotary(npy(k), cos, sin)))
+
+    def silu_mul(gate, up, out):
+        out.copy_(torch.from_numpy(oracle.llama_ref.silu_mul(npy(gate), npy(up))))
+
+    _lib.add_rmsnorm, _lib.rope, _lib.silu_mul = add_rmsnorm, rope, silu_mul
+    llama_mod._check_device = lambda *tensors: None
+    llama_mod.attention = attention
     sp._pack_wire = pack_wire
     sp._unpack_wire = unpack_wire
     sp.attend_into = attend_into
@@ -128,6 +147,28 @@ def wire_ring_worker(rank, world, case):
     ql, kl, vl, pl = (layout.shard(t, rank) for t in (q, k, v, pos))
     out = ring_attention(ql, kl, vl, pl, pl, ctx.sp, layout.sizes, causal=True)
     return out.numpy(), ctx.stats.total_bytes
+
+
+def llama_worker(rank, world, gold, name):
+    """The LLaMA prefill / greedy-decode path over gloo ranks (compute by the oracle) on the reference engine's
+    golden model: logits at every position and generated tokens with their logits."""
+    import json
+
+    install_oracle_compute()
+    from collaborative_edge_system_b200 import ParallelContext
+    from collaborative_edge_system_b200.llama import LlamaConfig, LlamaModel, forward_logits, generate_greedy
+
+    pc = json.loads(str(gold[f"{name}/meta"]))["parallel"]
+    cfg = LlamaConfig.from_dict(json.loads(str(gold["config"])))
+    sd = {k[len("weights/"):]: torch.from_numpy(v) for k, v in gold.items() if k.startswith("weights/")}
+    model = LlamaModel.from_state_dict(cfg, sd, dtype=torch.float64, device=torch.device("cpu"))
+    ctx = ParallelContext(1, world, 1)
+    kw = dict(sp_mode=pc.get("sp_mode", "ring"), sp_layout=pc.get("sp_layout", "contiguous"),
+              sp_weights=pc.get("sp_weights"))
+    logits = forward_logits(model, torch.from_numpy(gold["ids"]), torch.from_numpy(gold["mask"]), ctx.sp, **kw)
+    prompts = json.loads(str(gold["prompts"]))
+    tokens, scores = generate_greedy(model, prompts, int(gold["new_tokens"]), ctx.sp, return_scores=True, **kw)
+    return logits.numpy(), tokens, scores.numpy()
 
 
 def golden_inputs():

@@ -223,3 +223,24 @@ def wire_ring_worker(rank, world, case):
     ql, kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (q, k, v, pos))
     out = cea.ring_attention(ql, kl, vl, pl, pl, ctx.sp, lay.sizes, causal=True)
     return out.cpu().numpy(), ctx.stats.total_bytes
+
+
+def llama_worker(rank, world, gold, name):
+    """The LLaMA prefill / greedy decode over NCCL ranks (float64, the reference engine's golden model)."""
+    import json
+
+    import collaborative_edge_system_b200 as cea
+    from collaborative_edge_system_b200.llama import LlamaConfig, LlamaModel, forward_logits, generate_greedy
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    pc = json.loads(str(gold[f"{name}/meta"]))["parallel"]
+    cfg = LlamaConfig.from_dict(json.loads(str(gold["config"])))
+    sd = {k[len("weights/"):]: torch.from_numpy(v) for k, v in gold.items() if k.startswith("weights/")}
+    model = LlamaModel.from_state_dict(cfg, sd, dtype=torch.float64, device=dev)
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    kw = dict(sp_mode=pc.get("sp_mode", "ring"), sp_layout=pc.get("sp_layout", "contiguous"),
+              sp_weights=pc.get("sp_weights"))
+    logits = forward_logits(model, torch.from_numpy(gold["ids"]), torch.from_numpy(gold["mask"]), ctx.sp, **kw)
+    prompts = json.loads(str(gold["prompts"]))
+    tokens, scores = generate_greedy(model, prompts, int(gold["new_tokens"]), ctx.sp, return_scores=True, **kw)
+    return logits.cpu().numpy(), tokens, scores.cpu().numpy()

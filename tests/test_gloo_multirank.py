@@ -107,3 +107,20 @@ def test_ring_with_compressed_wire_matches_reference(golden_wire, name):
         tol = (1e-12 if m["dtype"] == "float64" else 2e-6) * max(1.0, float(np.abs(want).max()))
         assert np.abs(out - want).max() <= tol, (r, np.abs(out - want).max())
         assert sent == int(case[f"r{r}/bytes"])
+
+
+LLAMA_CASES = [("sp1", 1), ("sp2_ring", 2), ("sp3_ring_zigzag_weighted", 3), ("sp2_ulysses", 2)]
+
+
+@pytest.mark.parametrize("name,world", LLAMA_CASES)
+def test_llama_sp_prefill_and_decode_match_reference_engine(golden_llama, name, world):
+    """The LLaMA path's orchestration (sharding, ring / Ulysses prefill into the KV cache, decode owner, head
+    gathering, last-token broadcast) against the reference engine's float64 logits and greedy tokens."""
+    want_logits = golden_llama[f"{name}/logits"]
+    want_tokens = golden_llama[f"{name}/tokens"].tolist()
+    mask = golden_llama["mask"].astype(bool)
+    for logits, tokens, scores in _run(W.llama_worker, world, golden_llama, name):
+        assert np.abs(logits - want_logits)[mask].max() < 1e-10
+        assert tokens == want_tokens
+        for b in range(len(tokens)):
+            assert np.abs(scores[b] - golden_llama[f"{name}/scores{b}"]).max() < 1e-10
