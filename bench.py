@@ -442,6 +442,60 @@ def bench_decode(cea, rank, world, dev):
     }
 
 
+# ----------------------------------------------------------------------------- ours: LLaMA-3-8B prefill (config 5)
+LLAMA_S = 32768
+
+
+def bench_llama(cea, rank, world, dev, steps, warmup):
+    """Config 5: a LLaMA-3-8B prefill of one 32768-token prompt with zigzag ring SP over the ranks.
+
+    Random bf16 weights generated on each GPU from per-tensor seeds (identical on every rank), token ids uniform
+    in the vocabulary.  One step is the whole model over this rank's shard (embedding, 32 decoder layers with
+    ring attention, final norm) plus the LM head on the last token, as the engine's prefill does.  Model FLOPs
+    per step: 2 x (projection weights) per token plus the causal attention's 4 D Hq per visible (q, k) pair.
+    """
+    from collaborative_edge_system_b200.llama import LlamaConfig, LlamaModel
+
+    cfg = LlamaConfig.llama3_8b()
+    model = LlamaModel.random(cfg, seed=0, dtype=torch.bfloat16, device=dev)
+    comm = cea.ParallelContext(1, world, 1, device=dev).sp
+    layout = cea.SequenceLayout(LLAMA_S, world, None, "zigzag")
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, cfg.vocab_size, (1, LLAMA_S), generator=g)
+    pos = torch.arange(LLAMA_S).view(1, LLAMA_S)
+    ids_l = layout.shard(ids, rank).to(dev).contiguous()
+    pos_l = layout.shard(pos, rank).to(dev).contiguous()
+    h, i = cfg.hidden_size, cfg.intermediate_size
+    per_tok = 2.0 * cfg.num_layers * (h * (cfg.q_size + 2 * cfg.kv_size) + cfg.q_size * h + 3 * h * i)
+    attn = cfg.num_layers * 4.0 * cfg.head_dim * cfg.num_heads * (LLAMA_S * (LLAMA_S + 1) / 2)
+    total_flops = per_tok * LLAMA_S + attn + 2.0 * h * cfg.vocab_size
+
+    def step():
+        hidden = model.prefill(ids_l, pos_l, comm, layout.sizes, sp_mode="ring")
+        return model.logits(hidden[:, -1:])
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.no_grad(), ClockSampler(dev.index) as clk:
+        for _ in range(warmup):
+            step()
+        clk.wait_first()
+        barrier(world)
+        start.record()
+        for _ in range(steps):
+            step()
+        end.record()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world, dev) / steps
+    return {"metric": "LLaMA-3-8B 32K-token prefill tokens/s", "value": LLAMA_S / (ms / 1e3), "unit": "tok/s",
+            "ms_per_step": ms, "model_tflops": total_flops / (ms / 1e3) / 1e12,
+            "flops_per_step": total_flops, "clocks": clk.summary(),
+            "config": {"workload": "LLaMA-3-8B prefill (config 5)", "batch": 1, "seq_len": LLAMA_S,
+                       "layers": cfg.num_layers, "hidden": h, "heads": cfg.num_heads, "kv_heads": cfg.num_kv_heads,
+                       "ffn": i, "vocab": cfg.vocab_size, "layout": "zigzag", "parallelism": f"sp{world}",
+                       "weights": "random bf16, N(0, 0.02^2), generated on the GPU"},
+            "weights_gb": model.parameter_bytes() / 1e9}
+
+
 # ----------------------------------------------------------------------------- CPU baseline (oracle)
 def cpu_baseline(seconds_target: float = 15.0):
     """The reference algorithm's CPU restatement on a bounded sample of the prefill workload.
@@ -522,6 +576,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-ulysses", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--llama", action="store_true",
+                    help="run config 5 instead (LLaMA-3-8B 32K-token prefill with ring SP) and print its line")
     ap.add_argument("--ncu-case", choices=["prefill", "decode"], default=None,
                     help="run a small case of one kernel for an ncu capture (no timing, no JSON line)")
     args = ap.parse_args()
@@ -557,6 +613,15 @@ def main():
     _lib.load()
     rank, world, dev = setup(args.gpus)
     warmup = max(3, args.warmup)
+    if args.llama:
+        res = bench_llama(cea, rank, world, dev, args.steps, warmup)
+        status = _lib.device_status(clear=True)
+        if rank == 0:
+            print(json.dumps({**res, "n_gpus": world, "steps": args.steps, "warmup": warmup, "higher_is_better": True,
+                              "scaling": "strong", "dtype": "bf16", "data": "synthetic", "device_status": status}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
     pre = bench_prefill(cea, rank, world, dev, args.steps, warmup)
     e2e = bench_prefill_e2e(cea, rank, world, dev, args.steps, warmup, pre["layout"], pre["tensors"], pre["comm"])
     del pre["tensors"]
