@@ -446,8 +446,9 @@ def bench_decode(cea, rank, world, dev):
 LLAMA_S = 32768
 
 
-def bench_llama(cea, rank, world, dev, steps, warmup):
-    """Config 5: a LLaMA-3-8B prefill of one 32768-token prompt with zigzag ring SP over the ranks.
+def bench_llama(cea, rank, world, dev, steps, warmup, tp_size=1):
+    """Config 5: a LLaMA-3-8B prefill of one 32768-token prompt with zigzag ring SP over the ranks (with
+    ``tp_size`` > 1, an sp x tp mesh: heads, MLP units and vocabulary split over each TP group).
 
     Random bf16 weights generated on each GPU from per-tensor seeds (identical on every rank), token ids uniform
     in the vocabulary.  One step is the whole model over this rank's shard (embedding, 32 decoder layers with
@@ -457,14 +458,17 @@ def bench_llama(cea, rank, world, dev, steps, warmup):
     from collaborative_edge_system_b200.llama import LlamaConfig, LlamaModel
 
     cfg = LlamaConfig.llama3_8b()
-    model = LlamaModel.random(cfg, seed=0, dtype=torch.bfloat16, device=dev)
-    comm = cea.ParallelContext(1, world, 1, device=dev).sp
-    layout = cea.SequenceLayout(LLAMA_S, world, None, "zigzag")
+    if world % tp_size:
+        raise SystemExit(f"--llama-tp {tp_size} does not divide {world} GPUs")
+    ctx = cea.ParallelContext(1, world // tp_size, tp_size, device=dev)
+    model = LlamaModel.random(cfg, seed=0, dtype=torch.bfloat16, device=dev, tp=ctx.tp)
+    comm = ctx.sp
+    layout = cea.SequenceLayout(LLAMA_S, comm.size, None, "zigzag")
     g = torch.Generator().manual_seed(5)
     ids = torch.randint(0, cfg.vocab_size, (1, LLAMA_S), generator=g)
     pos = torch.arange(LLAMA_S).view(1, LLAMA_S)
-    ids_l = layout.shard(ids, rank).to(dev).contiguous()
-    pos_l = layout.shard(pos, rank).to(dev).contiguous()
+    ids_l = layout.shard(ids, comm.rank).to(dev).contiguous()
+    pos_l = layout.shard(pos, comm.rank).to(dev).contiguous()
     h, i = cfg.hidden_size, cfg.intermediate_size
     per_tok = 2.0 * cfg.num_layers * (h * (cfg.q_size + 2 * cfg.kv_size) + cfg.q_size * h + 3 * h * i)
     attn = cfg.num_layers * 4.0 * cfg.head_dim * cfg.num_heads * (LLAMA_S * (LLAMA_S + 1) / 2)
@@ -491,7 +495,8 @@ def bench_llama(cea, rank, world, dev, steps, warmup):
             "flops_per_step": total_flops, "clocks": clk.summary(),
             "config": {"workload": "LLaMA-3-8B prefill (config 5)", "batch": 1, "seq_len": LLAMA_S,
                        "layers": cfg.num_layers, "hidden": h, "heads": cfg.num_heads, "kv_heads": cfg.num_kv_heads,
-                       "ffn": i, "vocab": cfg.vocab_size, "layout": "zigzag", "parallelism": f"sp{world}",
+                       "ffn": i, "vocab": cfg.vocab_size, "layout": "zigzag",
+                       "parallelism": f"sp{comm.size}" + (f"xtp{tp_size}" if tp_size > 1 else ""),
                        "weights": "random bf16, N(0, 0.02^2), generated on the GPU"},
             "weights_gb": model.parameter_bytes() / 1e9}
 
@@ -578,6 +583,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--llama", action="store_true",
                     help="run config 5 instead (LLaMA-3-8B 32K-token prefill with ring SP) and print its line")
+    ap.add_argument("--llama-tp", type=int, default=1, help="tensor-parallel size of the --llama run")
     ap.add_argument("--ncu-case", choices=["prefill", "decode"], default=None,
                     help="run a small case of one kernel for an ncu capture (no timing, no JSON line)")
     args = ap.parse_args()
@@ -614,7 +620,7 @@ def main():
     rank, world, dev = setup(args.gpus)
     warmup = max(3, args.warmup)
     if args.llama:
-        res = bench_llama(cea, rank, world, dev, args.steps, warmup)
+        res = bench_llama(cea, rank, world, dev, args.steps, warmup, args.llama_tp)
         status = _lib.device_status(clear=True)
         if rank == 0:
             print(json.dumps({**res, "n_gpus": world, "steps": args.steps, "warmup": warmup, "higher_is_better": True,

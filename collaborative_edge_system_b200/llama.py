@@ -23,8 +23,9 @@ padding), the prompt sharded over the SP group by :class:`SequenceLayout`, the d
 from __future__ import annotations
 
 import math
+import zlib
 from dataclasses import dataclass, field, fields
-from typing import Any, Dict, List, Mapping, Optional, Sequence
+from typing import Any, Dict, List, Mapping, Optional, Sequence, Tuple
 
 import torch
 import torch.nn.functional as F
@@ -33,7 +34,7 @@ from . import _lib
 from .attention import attention, gqa_group
 from .cache import KVCache, assign_tokens, ring_decode_attention
 from .comm import Communicator
-from .partition import HeadShard, SequenceLayout, partition_heads
+from .partition import HeadShard, SequenceLayout, offsets_of, partition_heads, split_sizes
 from .sequence_parallel import gather_heads, gather_sequence, ring_attention, ulysses_attention
 
 
@@ -136,13 +137,66 @@ class LayerWeights:
     down_bias: Optional[torch.Tensor] = None
 
 
+@dataclass
+class TPShard:
+    """This rank's share of a tensor-parallel stage (``LlamaStage.__init__``, ``llama.py:353-390``): its query /
+    KV heads, MLP units and vocabulary rows, and the TP group that sums the row-parallel partials."""
+
+    comm: Optional[Communicator]
+    heads: HeadShard
+    ffn: Tuple[int, int]  # (start, count)
+    vocab: Tuple[int, int]  # (start, count)
+    vocab_sizes: List[int]
+
+    @classmethod
+    def of(cls, config: LlamaConfig, comm: Optional[Communicator], weights: Optional[Sequence[float]] = None
+           ) -> "TPShard":
+        n, r = (1, 0) if comm is None else (comm.size, comm.rank)
+        parts = list(weights) if weights is not None else n
+        heads = partition_heads(config.num_heads, config.num_kv_heads, parts)[r]
+        ffn_sizes = split_sizes(config.intermediate_size, parts)
+        vocab_sizes = split_sizes(config.vocab_size, parts)
+        return cls(comm if n > 1 else None, heads, (offsets_of(ffn_sizes)[r], ffn_sizes[r]),
+                   (offsets_of(vocab_sizes)[r], vocab_sizes[r]), vocab_sizes)
+
+
+def _param_shapes(config: LlamaConfig) -> Dict[str, Tuple[Tuple[int, ...], bool]]:
+    """Hugging Face parameter names of a full checkpoint -> (shape, is a norm weight)."""
+    c = config
+    h, i = c.hidden_size, c.intermediate_size
+    shapes: Dict[str, Tuple[Tuple[int, ...], bool]] = {"model.embed_tokens.weight": ((c.vocab_size, h), False)}
+    for layer in range(c.num_layers):
+        p = f"model.layers.{layer}."
+        for n, rows in (("q", c.q_size), ("k", c.kv_size), ("v", c.kv_size)):
+            shapes[p + f"self_attn.{n}_proj.weight"] = ((rows, h), False)
+            if c.qkv_bias:
+                shapes[p + f"self_attn.{n}_proj.bias"] = ((rows,), False)
+        shapes[p + "self_attn.o_proj.weight"] = ((h, c.q_size), False)
+        if c.o_bias:
+            shapes[p + "self_attn.o_proj.bias"] = ((h,), False)
+        for n, shape in (("gate", (i, h)), ("up", (i, h)), ("down", (h, i))):
+            shapes[p + f"mlp.{n}_proj.weight"] = (shape, False)
+            if c.mlp_bias:
+                shapes[p + f"mlp.{n}_proj.bias"] = ((shape[0],), False)
+        shapes[p + "input_layernorm.weight"] = ((h,), True)
+        shapes[p + "post_attention_layernorm.weight"] = ((h,), True)
+    shapes["model.norm.weight"] = ((h,), True)
+    if not c.tie_word_embeddings:
+        shapes["lm_head.weight"] = ((c.vocab_size, h), False)
+    return shapes
+
+
 class LlamaModel:
-    """A LLaMA-family model held on one GPU (every SP rank holds the whole stage, as in the reference)."""
+    """A LLaMA-family model stage held on one GPU: every SP rank holds the whole stage (as in the reference),
+    and with tensor parallelism every TP rank holds its :class:`TPShard` of it."""
 
     def __init__(self, config: LlamaConfig, embed: torch.Tensor, layers: List[LayerWeights], norm: torch.Tensor,
-                 lm_head: torch.Tensor) -> None:
+                 lm_head: torch.Tensor, shard: Optional[TPShard] = None) -> None:
         self.config = config
         self.embed, self.layers, self.norm, self.lm_head = embed, layers, norm, lm_head
+        self.shard = shard if shard is not None else TPShard.of(config, None)
+        self.tp = self.shard.comm
+        self.kv_map = _local_kv_map(self.shard.heads)
         self.dtype, self.device = embed.dtype, embed.device
         _check_device(embed)
         self.inv_freq = config.rope_inv_freq(torch.float64 if self.dtype == torch.float64 else torch.float32).to(
@@ -150,63 +204,72 @@ class LlamaModel:
 
     # ------------------------------------------------------------------ construction
     @classmethod
-    def from_state_dict(cls, config: LlamaConfig, sd: Mapping[str, torch.Tensor], *, dtype: torch.dtype,
-                        device: torch.device) -> "LlamaModel":
-        """From a full checkpoint with Hugging Face names (the names ``LlamaStage.load_weights`` reads,
-        ``llama.py:415-444``)."""
+    def _build(cls, config: LlamaConfig, get, tp: Optional[Communicator], tp_weights) -> "LlamaModel":
+        """This rank's (TP-sharded) weights from ``get(name)``, the full tensor of a Hugging Face parameter name;
+        the slicing follows the reference's ``load_full`` methods (``tensor_parallel.py:140-150,190-198,240-243,
+        281-296``)."""
+        c = config
+        sh = TPShard.of(c, tp, tp_weights)
+        d, me = c.head_dim, sh.heads
+        qs, qn = me.q_start * d, me.q_count * d
+        ks, kn = me.kv_start * d, me.kv_count * d
+        fs, fn = sh.ffn
+        vs, vn = sh.vocab
 
-        def get(name: str) -> torch.Tensor:
-            return sd[name].to(device=device, dtype=dtype).contiguous()
+        def rows(t: torch.Tensor, start: int, count: int) -> torch.Tensor:
+            return t.narrow(0, start, count)
 
-        def opt(name: str, on: bool) -> Optional[torch.Tensor]:
-            return get(name) if on else None
+        def cols(t: torch.Tensor, start: int, count: int) -> torch.Tensor:
+            return t.narrow(1, start, count).contiguous()
 
-        def cat(names: Sequence[str], on: bool = True) -> Optional[torch.Tensor]:
-            return torch.cat([get(n) for n in names]).contiguous() if on else None
+        def fused(prefix: str, suffix: str, spans, on: bool = True) -> Optional[torch.Tensor]:
+            if not on:
+                return None
+            return torch.cat([rows(get(prefix + n + suffix), a, b) for n, a, b in spans]).contiguous()
 
         layers = []
-        for i in range(config.num_layers):
-            p = f"model.layers.{i}."
-            qkv = [p + f"self_attn.{n}_proj" for n in "qkv"]
-            gu = [p + f"mlp.{n}_proj" for n in ("gate", "up")]
+        for layer in range(c.num_layers):
+            p = f"model.layers.{layer}."
+            qkv = [("q", qs, qn), ("k", ks, kn), ("v", ks, kn)]
+            gu = [("gate", fs, fn), ("up", fs, fn)]
             layers.append(LayerWeights(
-                qkv=cat([n + ".weight" for n in qkv]), o=get(p + "self_attn.o_proj.weight"),
-                gate_up=cat([n + ".weight" for n in gu]), down=get(p + "mlp.down_proj.weight"),
+                qkv=fused(p + "self_attn.", "_proj.weight", qkv),
+                o=cols(get(p + "self_attn.o_proj.weight"), qs, qn),
+                gate_up=fused(p + "mlp.", "_proj.weight", gu),
+                down=cols(get(p + "mlp.down_proj.weight"), fs, fn),
                 ln_in=get(p + "input_layernorm.weight"), ln_post=get(p + "post_attention_layernorm.weight"),
-                qkv_bias=cat([n + ".bias" for n in qkv], config.qkv_bias),
-                o_bias=opt(p + "self_attn.o_proj.bias", config.o_bias),
-                gate_up_bias=cat([n + ".bias" for n in gu], config.mlp_bias),
-                down_bias=opt(p + "mlp.down_proj.bias", config.mlp_bias)))
-        embed = get("model.embed_tokens.weight")
-        head = embed if config.tie_word_embeddings else get("lm_head.weight")
-        return cls(config, embed, layers, get("model.norm.weight"), head)
+                qkv_bias=fused(p + "self_attn.", "_proj.bias", qkv, c.qkv_bias),
+                o_bias=get(p + "self_attn.o_proj.bias") if c.o_bias else None,
+                gate_up_bias=fused(p + "mlp.", "_proj.bias", gu, c.mlp_bias),
+                down_bias=get(p + "mlp.down_proj.bias") if c.mlp_bias else None))
+        embed = rows(get("model.embed_tokens.weight"), vs, vn).contiguous()
+        head = embed if c.tie_word_embeddings else rows(get("lm_head.weight"), vs, vn).contiguous()
+        return cls(c, embed, layers, get("model.norm.weight"), head, sh)
+
+    @classmethod
+    def from_state_dict(cls, config: LlamaConfig, sd: Mapping[str, torch.Tensor], *, dtype: torch.dtype,
+                        device: torch.device, tp: Optional[Communicator] = None,
+                        tp_weights: Optional[Sequence[float]] = None) -> "LlamaModel":
+        """From a full checkpoint with Hugging Face names (the names ``LlamaStage.load_weights`` reads,
+        ``llama.py:415-444``); with a TP group, this rank's shard of it."""
+        return cls._build(config, lambda n: sd[n].to(device=device, dtype=dtype), tp, tp_weights)
 
     @classmethod
     def random(cls, config: LlamaConfig, *, seed: int = 0, dtype: torch.dtype = torch.bfloat16,
-               device: torch.device, std: float = 0.02) -> "LlamaModel":
-        """Random weights generated on the GPU, tensor by tensor from per-tensor seeds (every rank that calls
-        this gets the same model without a host copy): projections N(0, std^2), norm weights 1 + N(0, 0.01)."""
-        counter = [seed * 1000003]
+               device: torch.device, std: float = 0.02, tp: Optional[Communicator] = None,
+               tp_weights: Optional[Sequence[float]] = None) -> "LlamaModel":
+        """Random weights generated on the GPU, each full tensor from a seed derived from its name (every rank
+        gets the same model whatever its TP layout, without a host copy): projections N(0, std^2), norm weights
+        1 + N(0, 0.01)."""
+        shapes = _param_shapes(config)
 
-        def rand(*shape: int, norm: bool = False) -> torch.Tensor:
-            counter[0] += 1
-            g = torch.Generator(device=device).manual_seed(counter[0])
+        def get(name: str) -> torch.Tensor:
+            shape, norm = shapes[name]
+            g = torch.Generator(device=device).manual_seed(seed * 1000003 + zlib.crc32(name.encode()))
             t = torch.randn(*shape, generator=g, device=device, dtype=torch.float32)
             return ((1.0 + 0.1 * t) if norm else t * std).to(dtype)
 
-        c = config
-        h, i = c.hidden_size, c.intermediate_size
-        layers = []
-        for _ in range(c.num_layers):
-            layers.append(LayerWeights(
-                qkv=rand(c.q_size + 2 * c.kv_size, h), o=rand(h, c.q_size), gate_up=rand(2 * i, h), down=rand(h, i),
-                ln_in=rand(h, norm=True), ln_post=rand(h, norm=True),
-                qkv_bias=rand(c.q_size + 2 * c.kv_size) if c.qkv_bias else None,
-                o_bias=rand(h) if c.o_bias else None,
-                gate_up_bias=rand(2 * i) if c.mlp_bias else None, down_bias=rand(h) if c.mlp_bias else None))
-        embed = rand(c.vocab_size, h)
-        head = embed if c.tie_word_embeddings else rand(c.vocab_size, h)
-        return cls(config, embed, layers, rand(h, norm=True), head)
+        return cls._build(config, get, tp, tp_weights)
 
     def parameter_bytes(self) -> int:
         ts = [self.embed, self.norm] + ([] if self.lm_head is self.embed else [self.lm_head])
@@ -215,45 +278,72 @@ class LlamaModel:
         return sum(t.numel() * t.element_size() for t in ts)
 
     # ------------------------------------------------------------------ forward pieces
+    def _reduce(self, partial: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+        """Row-parallel partial sums summed over the TP group, then the bias (``tensor_parallel.py:67-80,181-187``)."""
+        out = self.tp.all_reduce(partial, compress=True) if self.tp is not None else partial
+        return out if bias is None else out + bias
+
+    def _embed(self, ids: torch.Tensor) -> torch.Tensor:
+        """Token embeddings; with TP each rank looks up its vocabulary rows and the group sums
+        (``VocabParallelEmbedding.forward``, ``tensor_parallel.py:231-242``)."""
+        if self.tp is None:
+            return F.embedding(ids, self.embed)
+        start, count = self.shard.vocab
+        outside = (ids < start) | (ids >= start + count)
+        out = F.embedding((ids - start).masked_fill(outside, 0), self.embed).masked_fill(outside.unsqueeze(-1), 0.0)
+        return self._reduce(out, None)
+
     def _qkv(self, L: LayerWeights, y: torch.Tensor, pos: torch.Tensor):
-        c = self.config
+        d, me = self.config.head_dim, self.shard.heads
         B, s, _ = y.shape
+        qn, kn = me.q_count * d, me.kv_count * d
         qkv = F.linear(y, L.qkv, L.qkv_bias)
-        q = qkv[..., : c.q_size].view(B, s, c.num_heads, c.head_dim)
-        k = qkv[..., c.q_size : c.q_size + c.kv_size].view(B, s, c.num_kv_heads, c.head_dim)
-        v = qkv[..., c.q_size + c.kv_size :].view(B, s, c.num_kv_heads, c.head_dim)
+        q = qkv[..., :qn].view(B, s, me.q_count, d)
+        k = qkv[..., qn : qn + kn].view(B, s, me.kv_count, d)
+        v = qkv[..., qn + kn :].view(B, s, me.kv_count, d)
         _lib.rope(q, k, pos, self.inv_freq)
         return q, k, v
 
     def _mlp(self, L: LayerWeights, y: torch.Tensor) -> torch.Tensor:
-        i = self.config.intermediate_size
+        i = self.shard.ffn[1]
         gu = F.linear(y, L.gate_up, L.gate_up_bias)
         act = torch.empty(gu.shape[:-1] + (i,), dtype=gu.dtype, device=gu.device)
         _lib.silu_mul(gu[..., :i], gu[..., i:], act)
-        return F.linear(act, L.down, L.down_bias)
+        return self._reduce(F.linear(act, L.down), L.down_bias)
 
     def _layers(self, ids: torch.Tensor, positions: torch.Tensor, attend) -> torch.Tensor:
         """Embedding, every decoder layer and the final norm (``DecoderLayer.forward``, ``llama.py:337-339``);
-        ``attend(layer_index, q, k, v)`` returns the attention output ``[B, s, Hq, D]`` of the roped q / k.
+        ``attend(layer_index, q, k, v)`` returns the attention output ``[B, s, Hq_local, D]`` of the roped q / k.
         Each residual add is fused into the RMSNorm that follows it."""
         eps = self.config.rms_norm_eps
-        resid = F.embedding(ids, self.embed)
+        resid = self._embed(ids)
         y = torch.empty_like(resid)
         delta = None
         for idx, L in enumerate(self.layers):
             _lib.add_rmsnorm(resid, delta, L.ln_in, y, eps)
             q, k, v = self._qkv(L, y, positions)
             B, s = q.shape[:2]
-            delta = F.linear(attend(idx, q, k, v).reshape(B, s, -1), L.o, L.o_bias)
+            delta = self._reduce(F.linear(attend(idx, q, k, v).reshape(B, s, -1), L.o), L.o_bias)
             _lib.add_rmsnorm(resid, delta, L.ln_post, y, eps)
             delta = self._mlp(L, y)
         _lib.add_rmsnorm(resid, delta, self.norm, y, eps)
         return y
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
-        return F.linear(hidden, self.lm_head)
+        """Full-vocabulary logits; with TP each rank projects its vocabulary rows and the group gathers them
+        (``ParallelLMHead``, ``tensor_parallel.py:256-261``)."""
+        out = F.linear(hidden, self.lm_head)
+        if self.tp is not None:
+            out = self.tp.all_gather(out, dim=-1, sizes=self.shard.vocab_sizes)
+        return out
 
     # ------------------------------------------------------------------ passes
+    def ulysses_shards(self, comm: Communicator, sp_weights: Optional[Sequence[float]] = None) -> List[HeadShard]:
+        """This TP rank's heads split over the SP group for Ulysses (``llama.py:128-131``)."""
+        me = self.shard.heads
+        parts = list(sp_weights) if sp_weights else comm.size
+        return partition_heads(me.q_count, me.kv_count, parts, kv_map=list(me.kv_map))
+
     def prefill(self, ids: torch.Tensor, positions: torch.Tensor, comm: Optional[Communicator],
                 seq_sizes: Optional[Sequence[int]] = None, *, sp_mode: str = "ring",
                 head_shards: Optional[Sequence[HeadShard]] = None, cache: Optional[KVCache] = None) -> torch.Tensor:
@@ -261,18 +351,18 @@ class LlamaModel:
         ``[B, s]``), attending over the whole prompt by ring or Ulysses SP (``llama.py:232-245``); with
         ``comm=None`` the tokens are all local.  With a ``cache`` every layer's K/V go into it: the rank's
         tokens (ring) or its head shard of every token (Ulysses)."""
-        c = self.config
         n = 1 if comm is None else comm.size
         seq_sizes = list(seq_sizes) if seq_sizes is not None else [ids.shape[1]] * n
         if sp_mode == "ulysses" and n > 1 and head_shards is None:
-            head_shards = partition_heads(c.num_heads, c.num_kv_heads, n)
+            head_shards = self.ulysses_shards(comm)
+        kv_map = self.kv_map
 
         def attend(idx, q, k, v):
             layer = cache.layer(idx) if cache is not None else None
             if n == 1:
-                o = attention(q, k, v, positions, positions, causal=True)
+                o = attention(q, k, v, positions, positions, causal=True, kv_map=kv_map)
             elif sp_mode == "ring":
-                o = ring_attention(q, k, v, positions, positions, comm, seq_sizes, causal=True)
+                o = ring_attention(q, k, v, positions, positions, comm, seq_sizes, causal=True, kv_map=kv_map)
             else:
                 o, (kh, vh, ph) = ulysses_attention(q, k, v, positions, comm, seq_sizes, head_shards, causal=True)
                 if layer is not None:
@@ -290,14 +380,15 @@ class LlamaModel:
         """Final hidden states ``[B, n, h]`` of tokens replicated on every SP rank, attending to the cache
         (``llama.py:247-267``): ring mode appends on the ``owner`` (with one rank, always) and merges the ranks'
         partials exactly; Ulysses mode appends each rank's head shard and gathers the heads."""
-        c = self.config
         if sp_mode == "ulysses" and comm.size > 1 and head_shards is None:
-            head_shards = partition_heads(c.num_heads, c.num_kv_heads, comm.size)
+            head_shards = self.ulysses_shards(comm)
+        kv_map, num_kv = self.kv_map, self.shard.heads.kv_count
 
         def attend(idx, q, k, v):
             layer = cache.layer(idx)
             if sp_mode == "ring" or comm.size == 1:
-                return ring_decode_attention(q, k, v, positions, layer, comm, owner, causal=True)
+                return ring_decode_attention(q, k, v, positions, layer, comm, owner, causal=True, kv_map=kv_map,
+                                             num_kv_heads=num_kv)
             me = head_shards[comm.rank]
             kvs = slice(me.kv_start, me.kv_start + me.kv_count)
             layer.append(k[:, :, kvs], v[:, :, kvs], positions)
@@ -354,8 +445,7 @@ def forward_logits(model: LlamaModel, input_ids: torch.Tensor, attention_mask: O
     if layout is None:  # too few tokens to shard: every rank computes them all
         return model.logits(model.prefill(ids, pos, None))
     ids_l, pos_l = layout.shard(ids, comm.rank), layout.shard(pos, comm.rank).contiguous()
-    shards = partition_heads(model.config.num_heads, model.config.num_kv_heads,
-                             list(sp_weights) if sp_weights else comm.size)
+    shards = model.ulysses_shards(comm, sp_weights) if sp_mode == "ulysses" else None
     h = model.prefill(ids_l, pos_l, comm, layout.sizes, sp_mode=sp_mode, head_shards=shards)
     return gather_sequence(model.logits(h), layout, comm)
 
@@ -370,8 +460,7 @@ def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new
     ids, pos = padded_batch(prompts, dev)
     B, S = ids.shape
     cache = KVCache(reserve_tokens=max(0, max_new_tokens - 1))
-    shards = partition_heads(model.config.num_heads, model.config.num_kv_heads,
-                             list(sp_weights) if sp_weights else comm.size)
+    shards = model.ulysses_shards(comm, sp_weights) if sp_mode == "ulysses" and comm.size > 1 else None
     next_pos = torch.tensor([len(p) for p in prompts], dtype=torch.long, device=dev)
     tokens: List[torch.Tensor] = []
     scores: List[torch.Tensor] = []
@@ -402,5 +491,5 @@ def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new
     return (out, torch.stack(scores, dim=1)) if return_scores else out
 
 
-__all__ = ["LayerWeights", "LlamaConfig", "LlamaModel", "forward_logits", "generate_greedy", "mask_positions",
+__all__ = ["LayerWeights", "LlamaConfig", "LlamaModel", "TPShard", "forward_logits", "generate_greedy", "mask_positions",
            "padded_batch"]

@@ -10,7 +10,10 @@ Builds a small LLaMA-architecture model (``ModelConfig.tiny`` with GQA, float64,
 * ``forward``: logits of a left-padded batch at every position, without and with ring / Ulysses sequence
   parallelism;
 * ``generate``: greedy tokens and the per-step logits, whose first step is the ring (or Ulysses) prefill into the
-  distributed KV cache and whose later steps decode against it.
+  distributed KV cache and whose later steps decode against it;
+
+each also with tensor parallelism (heads, MLP units and the vocabulary split over the TP group, one all-reduce
+after the O and down projections and after the embedding), alone and combined with ring or Ulysses SP.
 
 Writes ``llama_sp.npz`` next to this script: the configuration, the weights (Hugging Face names), the prompts, and
 each case's outputs.
@@ -36,6 +39,10 @@ CASES = [
     ("sp2_ring", 2, dict(sp_size=2)),
     ("sp3_ring_zigzag_weighted", 3, dict(sp_size=3, sp_layout="zigzag", sp_weights=[3, 2, 1])),
     ("sp2_ulysses", 2, dict(sp_size=2, sp_mode="ulysses")),
+    ("tp2", 2, dict(tp_size=2)),
+    ("tp3_uneven_heads", 3, dict(tp_size=3)),
+    ("tp2_sp2_ring", 4, dict(tp_size=2, sp_size=2)),
+    ("tp2_sp2_ulysses", 4, dict(tp_size=2, sp_size=2, sp_mode="ulysses")),
 ]
 
 

@@ -236,8 +236,8 @@ def llama_worker(rank, world, gold, name):
     pc = json.loads(str(gold[f"{name}/meta"]))["parallel"]
     cfg = LlamaConfig.from_dict(json.loads(str(gold["config"])))
     sd = {k[len("weights/"):]: torch.from_numpy(v) for k, v in gold.items() if k.startswith("weights/")}
-    model = LlamaModel.from_state_dict(cfg, sd, dtype=torch.float64, device=dev)
-    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    ctx = cea.ParallelContext(1, pc.get("sp_size", 1), pc.get("tp_size", 1), device=dev)
+    model = LlamaModel.from_state_dict(cfg, sd, dtype=torch.float64, device=dev, tp=ctx.tp)
     kw = dict(sp_mode=pc.get("sp_mode", "ring"), sp_layout=pc.get("sp_layout", "contiguous"),
               sp_weights=pc.get("sp_weights"))
     logits = forward_logits(model, torch.from_numpy(gold["ids"]), torch.from_numpy(gold["mask"]), ctx.sp, **kw)

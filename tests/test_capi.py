@@ -29,7 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.cea_abi_version() == _lib.ABI_VERSION == 4
+    assert lib.cea_abi_version() == _lib.ABI_VERSION == 5
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
@@ -91,6 +91,32 @@ def test_kv_append_rejects_bad_arguments_without_a_gpu():
     assert lib.cea_kv_append(ctypes.byref(kp), None) == _lib.CEA_OK
 
 
+def test_decoder_ops_reject_bad_arguments_without_a_gpu():
+    lib = _lib.load()
+    assert lib.cea_add_rmsnorm(None, None) == _lib.CEA_ERR_INVALID
+    rp = _lib.RmsNormParams()
+    rp.rows, rp.h, rp.eps, rp.dtype = 4, 0, 1e-5, _lib.BF16
+    assert lib.cea_add_rmsnorm(ctypes.byref(rp), None) == _lib.CEA_ERR_INVALID  # h = 0
+    rp.h = 64
+    assert lib.cea_add_rmsnorm(ctypes.byref(rp), None) == _lib.CEA_ERR_INVALID  # null tensors
+    rp.rows = 0
+    assert lib.cea_add_rmsnorm(ctypes.byref(rp), None) == _lib.CEA_OK  # nothing to do
+    assert lib.cea_rope(None, None) == _lib.CEA_ERR_INVALID
+    qp = _lib.RopeParams()
+    qp.B, qp.S, qp.Hq, qp.Hk, qp.D, qp.dtype = 1, 4, 2, 1, 7, _lib.BF16  # odd head size
+    assert lib.cea_rope(ctypes.byref(qp), None) == _lib.CEA_ERR_INVALID
+    qp.D = 8
+    assert lib.cea_rope(ctypes.byref(qp), None) == _lib.CEA_ERR_INVALID  # null tensors
+    qp.S = 0
+    assert lib.cea_rope(ctypes.byref(qp), None) == _lib.CEA_OK
+    assert lib.cea_silu_mul(None, None) == _lib.CEA_ERR_INVALID
+    sp = _lib.SiluMulParams()
+    sp.rows, sp.n, sp.dtype = 3, 5, _lib.F32
+    assert lib.cea_silu_mul(ctypes.byref(sp), None) == _lib.CEA_ERR_INVALID
+    sp.n = 0
+    assert lib.cea_silu_mul(ctypes.byref(sp), None) == _lib.CEA_OK
+
+
 def test_wire_cast_rejects_bad_arguments_without_a_gpu():
     lib = _lib.load()
     assert lib.cea_wire_cast(None, None) == _lib.CEA_ERR_INVALID
@@ -142,6 +168,13 @@ int main(void) {
   printf("cea_wire_cast_params %zu\n", sizeof(cea_wire_cast_params));
   P(cea_wire_cast_params, dst); P(cea_wire_cast_params, src_stride); P(cea_wire_cast_params, dst_stride);
   P(cea_wire_cast_params, B); P(cea_wire_cast_params, dst_dtype);
+  printf("cea_rmsnorm_params %zu\n", sizeof(cea_rmsnorm_params));
+  P(cea_rmsnorm_params, rows); P(cea_rmsnorm_params, eps); P(cea_rmsnorm_params, dtype);
+  printf("cea_rope_params %zu\n", sizeof(cea_rope_params));
+  P(cea_rope_params, k_stride); P(cea_rope_params, pos_stride); P(cea_rope_params, inv_freq);
+  P(cea_rope_params, D); P(cea_rope_params, dtype);
+  printf("cea_silu_mul_params %zu\n", sizeof(cea_silu_mul_params));
+  P(cea_silu_mul_params, rows); P(cea_silu_mul_params, out_stride); P(cea_silu_mul_params, dtype);
   return 0;
 }
 """
@@ -165,11 +198,15 @@ def test_struct_layout_matches_ctypes():
     assert c["cea_peer_merge_params"] == ctypes.sizeof(_lib.PeerMergeParams)
     assert c["cea_kv_append_params"] == ctypes.sizeof(_lib.KvAppendParams)
     assert c["cea_wire_cast_params"] == ctypes.sizeof(_lib.WireCastParams)
+    assert c["cea_rmsnorm_params"] == ctypes.sizeof(_lib.RmsNormParams)
+    assert c["cea_rope_params"] == ctypes.sizeof(_lib.RopeParams)
+    assert c["cea_silu_mul_params"] == ctypes.sizeof(_lib.SiluMulParams)
     for key, val in c.items():
         if "." in key:
             struct, field = key.split(".")
             cls = {"cea_attn_params": _lib.AttnParams, "cea_merge_params": _lib.MergeParams,
                    "cea_segment": _lib.Segment, "cea_copy_params": _lib.CopyParams,
                    "cea_peer_merge_params": _lib.PeerMergeParams, "cea_kv_append_params": _lib.KvAppendParams,
-                   "cea_wire_cast_params": _lib.WireCastParams}[struct]
+                   "cea_wire_cast_params": _lib.WireCastParams, "cea_rmsnorm_params": _lib.RmsNormParams,
+                   "cea_rope_params": _lib.RopeParams, "cea_silu_mul_params": _lib.SiluMulParams}[struct]
             assert getattr(cls, field).offset == val, key

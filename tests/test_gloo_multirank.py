@@ -109,13 +109,15 @@ def test_ring_with_compressed_wire_matches_reference(golden_wire, name):
         assert sent == int(case[f"r{r}/bytes"])
 
 
-LLAMA_CASES = [("sp1", 1), ("sp2_ring", 2), ("sp3_ring_zigzag_weighted", 3), ("sp2_ulysses", 2)]
+LLAMA_CASES = [("sp1", 1), ("sp2_ring", 2), ("sp3_ring_zigzag_weighted", 3), ("sp2_ulysses", 2), ("tp2", 2),
+               ("tp3_uneven_heads", 3), ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4)]
 
 
 @pytest.mark.parametrize("name,world", LLAMA_CASES)
 def test_llama_sp_prefill_and_decode_match_reference_engine(golden_llama, name, world):
-    """The LLaMA path's orchestration (sharding, ring / Ulysses prefill into the KV cache, decode owner, head
-    gathering, last-token broadcast) against the reference engine's float64 logits and greedy tokens."""
+    """The LLaMA path's orchestration (sequence sharding, ring / Ulysses prefill into the KV cache, decode owner,
+    head gathering, last-token broadcast; tensor-parallel heads, MLP units and vocabulary with their all-reduces)
+    against the reference engine's float64 logits and greedy tokens."""
     want_logits = golden_llama[f"{name}/logits"]
     want_tokens = golden_llama[f"{name}/tokens"].tolist()
     mask = golden_llama["mask"].astype(bool)

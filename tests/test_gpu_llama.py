@@ -148,7 +148,9 @@ def _gpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.mark.parametrize("name,world", [("sp2_ring", 2), ("sp2_ulysses", 2), ("sp3_ring_zigzag_weighted", 3)])
+@pytest.mark.parametrize("name,world", [("sp2_ring", 2), ("sp2_ulysses", 2), ("tp2", 2),
+                                        ("sp3_ring_zigzag_weighted", 3), ("tp3_uneven_heads", 3),
+                                        ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4)])
 def test_llama_sp_multi_gpu_matches_reference_engine(golden_llama, name, world):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
