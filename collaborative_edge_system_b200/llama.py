@@ -311,23 +311,33 @@ class LlamaModel:
         _lib.silu_mul(gu[..., :i], gu[..., i:], act)
         return self._reduce(F.linear(act, L.down), L.down_bias)
 
-    def _layers(self, ids: torch.Tensor, positions: torch.Tensor, attend) -> torch.Tensor:
-        """Embedding, every decoder layer and the final norm (``DecoderLayer.forward``, ``llama.py:337-339``);
-        ``attend(layer_index, q, k, v)`` returns the attention output ``[B, s, Hq_local, D]`` of the roped q / k.
-        Each residual add is fused into the RMSNorm that follows it."""
+    def _layers(self, ids: torch.Tensor, attn_block, mlp_block=None) -> torch.Tensor:
+        """Embedding, every decoder layer and the final norm (``DecoderLayer.forward``, ``llama.py:337-339``).
+        ``attn_block(layer_index, weights, y)`` and ``mlp_block(weights, y)`` return the (reduced) output of the
+        attention and MLP blocks on the normalised input ``y``; each residual add is fused into the RMSNorm that
+        follows it."""
         eps = self.config.rms_norm_eps
+        mlp_block = mlp_block or self._mlp
         resid = self._embed(ids)
         y = torch.empty_like(resid)
         delta = None
         for idx, L in enumerate(self.layers):
             _lib.add_rmsnorm(resid, delta, L.ln_in, y, eps)
-            q, k, v = self._qkv(L, y, positions)
-            B, s = q.shape[:2]
-            delta = self._reduce(F.linear(attend(idx, q, k, v).reshape(B, s, -1), L.o), L.o_bias)
+            delta = attn_block(idx, L, y)
             _lib.add_rmsnorm(resid, delta, L.ln_post, y, eps)
-            delta = self._mlp(L, y)
+            delta = mlp_block(L, y)
         _lib.add_rmsnorm(resid, delta, self.norm, y, eps)
         return y
+
+    def _attn_block(self, attend, positions: torch.Tensor):
+        """The attention block: fused QKV GEMM, rotary, ``attend(layer_index, q, k, v)``, O GEMM + TP reduction."""
+
+        def block(idx, L, y):
+            q, k, v = self._qkv(L, y, positions)
+            B, s = q.shape[:2]
+            return self._reduce(F.linear(attend(idx, q, k, v).reshape(B, s, -1), L.o), L.o_bias)
+
+        return block
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Full-vocabulary logits; with TP each rank projects its vocabulary rows and the group gathers them
@@ -372,16 +382,26 @@ class LlamaModel:
                 layer.append(k, v, positions)  # the cache stays sharded along the sequence
             return o
 
-        return self._layers(ids, positions, attend)
+        return self._layers(ids, self._attn_block(attend, positions))
 
     def decode(self, ids: torch.Tensor, positions: torch.Tensor, comm: Communicator, cache: KVCache,
                owner: Optional[int], *, sp_mode: str = "ring",
-               head_shards: Optional[Sequence[HeadShard]] = None) -> torch.Tensor:
+               head_shards: Optional[Sequence[HeadShard]] = None, sp_split: bool = False,
+               stage: Optional[Communicator] = None, sp_weights: Optional[Sequence[float]] = None) -> torch.Tensor:
         """Final hidden states ``[B, n, h]`` of tokens replicated on every SP rank, attending to the cache
         (``llama.py:247-267``): ring mode appends on the ``owner`` (with one rank, always) and merges the ranks'
-        partials exactly; Ulysses mode appends each rank's head shard and gathers the heads."""
+        partials exactly; Ulysses mode appends each rank's head shard and gathers the heads.
+
+        With ``sp_split`` (``ParallelConfig.sp_decode_split``, ``llama.py:181-220,308-318``) the SP ranks share the
+        dense work of every layer instead of repeating it: each projects and attends for its slice of the heads
+        and computes its slice of the MLP units, and one all-reduce over the ``stage`` group (SP x TP) sums the
+        partial projections."""
         if sp_mode == "ulysses" and comm.size > 1 and head_shards is None:
-            head_shards = self.ulysses_shards(comm)
+            head_shards = self.ulysses_shards(comm, sp_weights)
+        if sp_split and comm.size > 1:
+            if stage is None:
+                raise ValueError("sp_split needs the stage communicator (SP x TP)")
+            return self._decode_sp_split(ids, positions, comm, cache, owner, sp_mode, head_shards, stage, sp_weights)
         kv_map, num_kv = self.kv_map, self.shard.heads.kv_count
 
         def attend(idx, q, k, v):
@@ -397,7 +417,91 @@ class LlamaModel:
                               kv_map=_local_kv_map(me))
             return gather_heads(local, comm, head_shards)
 
-        return self._layers(ids, positions, attend)
+        return self._layers(ids, self._attn_block(attend, positions))
+
+    def _decode_sp_split(self, ids, positions, comm, cache, owner, sp_mode, head_shards, stage, sp_weights):
+        c, d, me = self.config, self.config.head_dim, self.shard.heads
+        parts = list(sp_weights) if sp_weights else comm.size
+        qn, kn = me.q_count * d, me.kv_count * d
+        # this rank's query heads (relative to the TP-local heads) and MLP units (relative to the TP-local units)
+        if sp_mode == "ulysses":
+            mine = head_shards[comm.rank]
+            heads: Optional[Tuple[int, int]] = (mine.q_start, mine.q_count)
+        elif me.q_count >= comm.size:
+            sizes = split_sizes(me.q_count, parts)
+            heads = (offsets_of(sizes)[comm.rank], sizes[comm.rank])
+        else:
+            heads = None
+        i_local = self.shard.ffn[1]
+        units = None
+        if i_local >= comm.size:
+            sizes = split_sizes(i_local, parts)
+            units = (offsets_of(sizes)[comm.rank], sizes[comm.rank])
+        kv_map, num_kv = self.kv_map, me.kv_count
+
+        def rows(L, y, a, b):
+            """Rows ``[a, b)`` of the fused QKV projection (weight views, no copy)."""
+            return F.linear(y, L.qkv[a:b], None if L.qkv_bias is None else L.qkv_bias[a:b])
+
+        def stage_reduce(partial, bias):
+            out = stage.all_reduce(partial, compress=True)  # sums the SP and TP partials at once
+            return out if bias is None else out + bias
+
+        def attn_block(idx, L, y):
+            if heads is None:  # too few heads to split: the whole-heads path of every rank
+                return self._attn_block(self._ring_decode_attend(comm, cache, owner, positions, kv_map, num_kv),
+                                        positions)(idx, L, y)
+            B, S = y.shape[:2]
+            layer = cache.layer(idx)
+            hs, hc = heads
+            if sp_mode == "ulysses":
+                # this rank projects, caches and attends for its heads only
+                u = head_shards[comm.rank]
+                lo, hi = u.kv_start * d, (u.kv_start + u.kv_count) * d
+                q = rows(L, y, u.q_start * d, (u.q_start + u.q_count) * d).view(B, S, u.q_count, d)
+                k = rows(L, y, qn + lo, qn + hi).view(B, S, u.kv_count, d)
+                v = rows(L, y, qn + kn + lo, qn + kn + hi).view(B, S, u.kv_count, d)
+                _lib.rope(q, k, positions, self.inv_freq)
+                layer.append(k, v, positions)
+                kc, vc, pc = layer.view()
+                local = attention(q, kc, vc, positions, pc, causal=True, kv_map=_local_kv_map(u))
+            else:
+                # ring: every rank needs all its query heads; only the cache owner needs K / V
+                q = rows(L, y, 0, qn).view(B, S, me.q_count, d)
+                k = v = None
+                if owner == comm.rank:
+                    kv = rows(L, y, qn, qn + 2 * kn).view(B, S, 2 * me.kv_count, d)
+                    k, v = kv[:, :, : me.kv_count], kv[:, :, me.kv_count :]
+                    _lib.rope(q, k, positions, self.inv_freq)
+                else:
+                    _lib.rope(q, q[:, :, :0], positions, self.inv_freq)
+                out = ring_decode_attention(q, k, v, positions, layer, comm, owner, causal=True, kv_map=kv_map,
+                                            num_kv_heads=num_kv)
+                local = out[:, :, hs : hs + hc]
+            partial = F.linear(local.reshape(B, S, hc * d), L.o[:, hs * d : (hs + hc) * d])
+            return stage_reduce(partial, L.o_bias)
+
+        def mlp_block(L, y):
+            if units is None:
+                return self._mlp(L, y)
+            a, n = units
+            gu_b = L.gate_up_bias
+            gate = F.linear(y, L.gate_up[a : a + n], None if gu_b is None else gu_b[a : a + n])
+            up = F.linear(y, L.gate_up[i_local + a : i_local + a + n],
+                          None if gu_b is None else gu_b[i_local + a : i_local + a + n])
+            act = torch.empty_like(gate)
+            _lib.silu_mul(gate, up, act)
+            return stage_reduce(F.linear(act, L.down[:, a : a + n]), L.down_bias)
+
+        return self._layers(ids, attn_block, mlp_block)
+
+    @staticmethod
+    def _ring_decode_attend(comm, cache, owner, positions, kv_map, num_kv):
+        def attend(idx, q, k, v):
+            return ring_decode_attention(q, k, v, positions, cache.layer(idx), comm, owner, causal=True,
+                                         kv_map=kv_map, num_kv_heads=num_kv)
+
+        return attend
 
 
 def _local_kv_map(shard: HeadShard) -> Optional[List[int]]:
@@ -452,10 +556,12 @@ def forward_logits(model: LlamaModel, input_ids: torch.Tensor, attention_mask: O
 
 def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new_tokens: int, comm: Communicator,
                     *, sp_mode: str = "ring", sp_layout: str = "contiguous",
-                    sp_weights: Optional[Sequence[float]] = None, return_scores: bool = False):
+                    sp_weights: Optional[Sequence[float]] = None, return_scores: bool = False,
+                    sp_decode_split: bool = False, stage: Optional[Communicator] = None):
     """Greedy generation over the SP group (``CollabEngine.generate`` with one micro-batch and no pipeline):
     the prompt is prefilled (sharded when it has at least as many tokens as ranks) into a :class:`KVCache`,
-    then every step decodes one token per sequence.  Returns the tokens (and the per-step logits)."""
+    then every step decodes one token per sequence; with ``sp_decode_split`` the replicated passes share each
+    layer's dense work over the ``stage`` group.  Returns the tokens (and the per-step logits)."""
     dev = model.device
     ids, pos = padded_batch(prompts, dev)
     B, S = ids.shape
@@ -474,7 +580,8 @@ def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new
         h_last = h[:, index].contiguous() if comm.rank == last_rank else h.new_empty((B, h.shape[-1]))
         h_last = comm.broadcast(h_last, src=last_rank)
     else:
-        h_last = model.decode(ids, pos, comm, cache, owner, sp_mode=sp_mode, head_shards=shards)[:, -1]
+        h_last = model.decode(ids, pos, comm, cache, owner, sp_mode=sp_mode, head_shards=shards,
+                              sp_split=sp_decode_split, stage=stage, sp_weights=sp_weights)[:, -1]
     for step in range(max_new_tokens):
         logits = model.logits(h_last)
         if return_scores:
@@ -485,7 +592,8 @@ def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new
             break
         owner = assign_tokens(cache, 1, comm.size, sp_mode=sp_mode)
         h_last = model.decode(tok.unsqueeze(1), next_pos.unsqueeze(1), comm, cache, owner, sp_mode=sp_mode,
-                              head_shards=shards)[:, -1]
+                              head_shards=shards, sp_split=sp_decode_split, stage=stage,
+                              sp_weights=sp_weights)[:, -1]
         next_pos = next_pos + 1
     out = torch.stack(tokens, dim=1).tolist()
     return (out, torch.stack(scores, dim=1)) if return_scores else out

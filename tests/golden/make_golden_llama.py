@@ -13,7 +13,8 @@ Builds a small LLaMA-architecture model (``ModelConfig.tiny`` with GQA, float64,
   distributed KV cache and whose later steps decode against it;
 
 each also with tensor parallelism (heads, MLP units and the vocabulary split over the TP group, one all-reduce
-after the O and down projections and after the embedding), alone and combined with ring or Ulysses SP.
+after the O and down projections and after the embedding), alone and combined with ring or Ulysses SP, and with
+``sp_decode_split`` (replicated tokens: the SP ranks share each layer's heads and MLP units).
 
 Writes ``llama_sp.npz`` next to this script: the configuration, the weights (Hugging Face names), the prompts, and
 each case's outputs.
@@ -43,6 +44,10 @@ CASES = [
     ("tp3_uneven_heads", 3, dict(tp_size=3)),
     ("tp2_sp2_ring", 4, dict(tp_size=2, sp_size=2)),
     ("tp2_sp2_ulysses", 4, dict(tp_size=2, sp_size=2, sp_mode="ulysses")),
+    ("sp2_ring_decode_split", 2, dict(sp_size=2, sp_decode_split=True)),
+    ("sp2_ulysses_decode_split", 2, dict(sp_size=2, sp_mode="ulysses", sp_decode_split=True)),
+    ("tp2_sp2_ring_decode_split", 4, dict(tp_size=2, sp_size=2, sp_decode_split=True)),
+    ("sp3_ring_weighted_decode_split", 3, dict(sp_size=3, sp_weights=[3, 2, 1], sp_decode_split=True)),
 ]
 
 

@@ -110,14 +110,17 @@ def test_ring_with_compressed_wire_matches_reference(golden_wire, name):
 
 
 LLAMA_CASES = [("sp1", 1), ("sp2_ring", 2), ("sp3_ring_zigzag_weighted", 3), ("sp2_ulysses", 2), ("tp2", 2),
-               ("tp3_uneven_heads", 3), ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4)]
+               ("tp3_uneven_heads", 3), ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4), ("sp2_ring_decode_split", 2),
+               ("sp2_ulysses_decode_split", 2), ("tp2_sp2_ring_decode_split", 4),
+               ("sp3_ring_weighted_decode_split", 3)]
 
 
 @pytest.mark.parametrize("name,world", LLAMA_CASES)
 def test_llama_sp_prefill_and_decode_match_reference_engine(golden_llama, name, world):
     """The LLaMA path's orchestration (sequence sharding, ring / Ulysses prefill into the KV cache, decode owner,
-    head gathering, last-token broadcast; tensor-parallel heads, MLP units and vocabulary with their all-reduces)
-    against the reference engine's float64 logits and greedy tokens."""
+    head gathering, last-token broadcast; tensor-parallel heads, MLP units and vocabulary with their all-reduces;
+    sp_decode_split's shared heads / units and stage all-reduce) against the reference engine's float64 logits and
+    greedy tokens."""
     want_logits = golden_llama[f"{name}/logits"]
     want_tokens = golden_llama[f"{name}/tokens"].tolist()
     mask = golden_llama["mask"].astype(bool)

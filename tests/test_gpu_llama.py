@@ -150,7 +150,9 @@ def _gpus():
 
 @pytest.mark.parametrize("name,world", [("sp2_ring", 2), ("sp2_ulysses", 2), ("tp2", 2),
                                         ("sp3_ring_zigzag_weighted", 3), ("tp3_uneven_heads", 3),
-                                        ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4)])
+                                        ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4), ("sp2_ring_decode_split", 2),
+                                        ("sp2_ulysses_decode_split", 2), ("tp2_sp2_ring_decode_split", 4),
+                                        ("sp3_ring_weighted_decode_split", 3)])
 def test_llama_sp_multi_gpu_matches_reference_engine(golden_llama, name, world):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")

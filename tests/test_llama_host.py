@@ -4,7 +4,6 @@ made by ``tests/golden/make_golden_rope.py``)."""
 import json
 
 
-
 def test_rope_inv_freq_matches_reference():
     """``LlamaConfig.rope_inv_freq`` (default, linear and llama3 scalings) equals the reference's
     ``ModelConfig.rope_inv_freq`` in float64 and float32."""
