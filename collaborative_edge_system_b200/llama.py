@@ -557,17 +557,26 @@ def forward_logits(model: LlamaModel, input_ids: torch.Tensor, attention_mask: O
 def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new_tokens: int, comm: Communicator,
                     *, sp_mode: str = "ring", sp_layout: str = "contiguous",
                     sp_weights: Optional[Sequence[float]] = None, return_scores: bool = False,
-                    sp_decode_split: bool = False, stage: Optional[Communicator] = None):
-    """Greedy generation over the SP group (``CollabEngine.generate`` with one micro-batch and no pipeline):
-    the prompt is prefilled (sharded when it has at least as many tokens as ranks) into a :class:`KVCache`,
-    then every step decodes one token per sequence; with ``sp_decode_split`` the replicated passes share each
-    layer's dense work over the ``stage`` group.  Returns the tokens (and the per-step logits)."""
+                    eos_token_id: Optional[int] = None, sp_decode_split: bool = False,
+                    stage: Optional[Communicator] = None):
+    """Greedy generation over the SP group (``CollabEngine.generate`` with one micro-batch and no pipeline,
+    ``engine.py:349-506``): the prompt is prefilled (sharded when it has at least as many tokens as ranks) into a
+    :class:`KVCache`, then every step decodes one token per sequence; with ``sp_decode_split`` the replicated
+    passes share each layer's dense work over the ``stage`` group.
+
+    With ``eos_token_id`` a finished sequence keeps emitting it, generation stops once every sequence has
+    finished, and each sequence is cut after its first one.  Returns the token lists, and with
+    ``return_scores`` also each sequence's per-step logits ``[len(tokens), vocab]``."""
+    n = len(prompts)
+    if max_new_tokens <= 0:
+        return ([[] for _ in range(n)], [None] * n) if return_scores else [[] for _ in range(n)]
     dev = model.device
     ids, pos = padded_batch(prompts, dev)
     B, S = ids.shape
     cache = KVCache(reserve_tokens=max(0, max_new_tokens - 1))
     shards = model.ulysses_shards(comm, sp_weights) if sp_mode == "ulysses" and comm.size > 1 else None
     next_pos = torch.tensor([len(p) for p in prompts], dtype=torch.long, device=dev)
+    done = torch.zeros(B, dtype=torch.bool, device=dev)
     tokens: List[torch.Tensor] = []
     scores: List[torch.Tensor] = []
     layout = _layout(S, comm, sp_layout, sp_weights)  # the cache is empty: a long enough prompt is sharded
@@ -587,8 +596,11 @@ def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new
         if return_scores:
             scores.append(logits)
         tok = logits.argmax(dim=-1)
+        if eos_token_id is not None:  # engine.py:287-289
+            tok = torch.where(done, torch.full_like(tok, eos_token_id), tok)
+            done |= tok == eos_token_id
         tokens.append(tok)
-        if step + 1 == max_new_tokens:
+        if step + 1 == max_new_tokens or (eos_token_id is not None and bool(done.all())):
             break
         owner = assign_tokens(cache, 1, comm.size, sp_mode=sp_mode)
         h_last = model.decode(tok.unsqueeze(1), next_pos.unsqueeze(1), comm, cache, owner, sp_mode=sp_mode,
@@ -596,7 +608,12 @@ def generate_greedy(model: LlamaModel, prompts: Sequence[Sequence[int]], max_new
                               sp_weights=sp_weights)[:, -1]
         next_pos = next_pos + 1
     out = torch.stack(tokens, dim=1).tolist()
-    return (out, torch.stack(scores, dim=1)) if return_scores else out
+    if eos_token_id is not None:  # engine.py:415-419
+        out = [seq[: seq.index(eos_token_id) + 1] if eos_token_id in seq else seq for seq in out]
+    if not return_scores:
+        return out
+    stacked = torch.stack(scores, dim=1)
+    return out, [stacked[b, : len(out[b])] for b in range(n)]
 
 
 __all__ = ["LayerWeights", "LlamaConfig", "LlamaModel", "TPShard", "forward_logits", "generate_greedy", "mask_positions",

@@ -167,9 +167,10 @@ def llama_worker(rank, world, gold, name):
               sp_weights=pc.get("sp_weights"))
     logits = forward_logits(model, torch.from_numpy(gold["ids"]), torch.from_numpy(gold["mask"]), ctx.sp, **kw)
     prompts = json.loads(str(gold["prompts"]))
+    gen = json.loads(str(gold[f"{name}/meta"])).get("generate", {})
     tokens, scores = generate_greedy(model, prompts, int(gold["new_tokens"]), ctx.sp, return_scores=True,
-                                     sp_decode_split=pc.get("sp_decode_split", False), stage=ctx.stage, **kw)
-    return logits.numpy(), tokens, scores.numpy()
+                                     sp_decode_split=pc.get("sp_decode_split", False), stage=ctx.stage, **gen, **kw)
+    return logits.numpy(), tokens, [sc.numpy() for sc in scores]
 
 
 def golden_inputs():

@@ -48,6 +48,9 @@ CASES = [
     ("sp2_ulysses_decode_split", 2, dict(sp_size=2, sp_mode="ulysses", sp_decode_split=True)),
     ("tp2_sp2_ring_decode_split", 4, dict(tp_size=2, sp_size=2, sp_decode_split=True)),
     ("sp3_ring_weighted_decode_split", 3, dict(sp_size=3, sp_weights=[3, 2, 1], sp_decode_split=True)),
+    # generation options: an end-of-sequence token that some sequences emit
+    ("sp1_eos", 1, {}, dict(eos_token_id=85)),
+    ("sp2_ring_eos", 2, dict(sp_size=2), dict(eos_token_id=85)),
 ]
 
 
@@ -67,7 +70,7 @@ def _padded(prompts):
     return ids, mask
 
 
-def _worker(rank, world, pc_dict):
+def _worker(rank, world, pc_dict, gen_kw):
     from collab_infer import CollabEngine, ModelConfig, ParallelConfig, random_state_dict
 
     cfg = ModelConfig.tiny(**MODEL)
@@ -75,7 +78,7 @@ def _worker(rank, world, pc_dict):
                        dtype=torch.float64)
     ids, mask = _padded(PROMPTS)
     logits = eng.forward(ids, mask, broadcast=True)
-    res = eng.generate(PROMPTS, max_new_tokens=NEW_TOKENS, return_scores=True)
+    res = eng.generate(PROMPTS, max_new_tokens=NEW_TOKENS, return_scores=True, **gen_kw)
     return {"logits": logits.numpy(), "tokens": res.tokens,
             "scores": [s.numpy() if s is not None else None for s in (res.scores or [])]}
 
@@ -92,12 +95,14 @@ def main(root: str) -> None:
         out[f"weights/{name}"] = t.numpy()
     ids, mask = _padded(PROMPTS)
     out["ids"], out["mask"] = ids.numpy(), mask.numpy()
-    for name, world, pc in CASES:
-        res = launch_local(_worker, world, args=(pc,), return_results=True, threads_per_rank=1, timeout_s=600)
+    for case in CASES:
+        name, world, pc = case[:3]
+        gen_kw = case[3] if len(case) > 3 else {}
+        res = launch_local(_worker, world, args=(pc, gen_kw), return_results=True, threads_per_rank=1, timeout_s=600)
         r0 = res[0]
-        out[f"{name}/meta"] = np.array(json.dumps({"world": world, "parallel": pc}))
+        out[f"{name}/meta"] = np.array(json.dumps({"world": world, "parallel": pc, "generate": gen_kw}))
         out[f"{name}/logits"] = r0["logits"]
-        out[f"{name}/tokens"] = np.array(r0["tokens"])
+        out[f"{name}/tokens"] = np.array(json.dumps(r0["tokens"]))  # ragged when sequences stop at EOS
         for b, sc in enumerate(r0["scores"]):
             out[f"{name}/scores{b}"] = sc
     np.savez_compressed(os.path.join(HERE, "llama_sp.npz"), **out)

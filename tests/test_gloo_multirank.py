@@ -1,6 +1,8 @@
 """Multi-rank host logic on gloo CPU ranks: the Communicator's uneven collectives and the
 ring / Ulysses / distributed-KV orchestration against the reference's golden vectors."""
 
+import json
+
 import numpy as np
 import pytest
 import torch
@@ -112,7 +114,7 @@ def test_ring_with_compressed_wire_matches_reference(golden_wire, name):
 LLAMA_CASES = [("sp1", 1), ("sp2_ring", 2), ("sp3_ring_zigzag_weighted", 3), ("sp2_ulysses", 2), ("tp2", 2),
                ("tp3_uneven_heads", 3), ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4), ("sp2_ring_decode_split", 2),
                ("sp2_ulysses_decode_split", 2), ("tp2_sp2_ring_decode_split", 4),
-               ("sp3_ring_weighted_decode_split", 3)]
+               ("sp3_ring_weighted_decode_split", 3), ("sp1_eos", 1), ("sp2_ring_eos", 2)]
 
 
 @pytest.mark.parametrize("name,world", LLAMA_CASES)
@@ -122,7 +124,7 @@ def test_llama_sp_prefill_and_decode_match_reference_engine(golden_llama, name, 
     sp_decode_split's shared heads / units and stage all-reduce) against the reference engine's float64 logits and
     greedy tokens."""
     want_logits = golden_llama[f"{name}/logits"]
-    want_tokens = golden_llama[f"{name}/tokens"].tolist()
+    want_tokens = json.loads(str(golden_llama[f"{name}/tokens"]))
     mask = golden_llama["mask"].astype(bool)
     for logits, tokens, scores in _run(W.llama_worker, world, golden_llama, name):
         assert np.abs(logits - want_logits)[mask].max() < 1e-10

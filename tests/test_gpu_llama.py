@@ -106,7 +106,8 @@ def _golden_model(gold, dtype=torch.float64):
     return LlamaModel.from_state_dict(cfg, sd, dtype=dtype, device=DEV)
 
 
-def test_llama_sp1_matches_reference_engine(golden_llama):
+@pytest.mark.parametrize("name", ["sp1", "sp1_eos"])
+def test_llama_sp1_matches_reference_engine(golden_llama, name):
     import collaborative_edge_system_b200 as cea
 
     model = _golden_model(golden_llama)
@@ -114,12 +115,13 @@ def test_llama_sp1_matches_reference_engine(golden_llama):
     logits = forward_logits(model, torch.from_numpy(golden_llama["ids"]), torch.from_numpy(golden_llama["mask"]),
                             comm)
     mask = golden_llama["mask"].astype(bool)
-    assert np.abs(logits.cpu().numpy() - golden_llama["sp1/logits"])[mask].max() < 1e-10
+    assert np.abs(logits.cpu().numpy() - golden_llama[f"{name}/logits"])[mask].max() < 1e-10
     prompts = json.loads(str(golden_llama["prompts"]))
-    tokens, scores = generate_greedy(model, prompts, int(golden_llama["new_tokens"]), comm, return_scores=True)
-    assert tokens == golden_llama["sp1/tokens"].tolist()
+    gen = json.loads(str(golden_llama[f"{name}/meta"])).get("generate", {})
+    tokens, scores = generate_greedy(model, prompts, int(golden_llama["new_tokens"]), comm, return_scores=True, **gen)
+    assert tokens == json.loads(str(golden_llama[f"{name}/tokens"]))
     for b in range(len(prompts)):
-        assert np.abs(scores[b].cpu().numpy() - golden_llama[f"sp1/scores{b}"]).max() < 1e-10
+        assert np.abs(scores[b].cpu().numpy() - golden_llama[f"{name}/scores{b}"]).max() < 1e-10
     assert _lib.device_status(clear=True) == 0
 
 
@@ -152,7 +154,7 @@ def _gpus():
                                         ("sp3_ring_zigzag_weighted", 3), ("tp3_uneven_heads", 3),
                                         ("tp2_sp2_ring", 4), ("tp2_sp2_ulysses", 4), ("sp2_ring_decode_split", 2),
                                         ("sp2_ulysses_decode_split", 2), ("tp2_sp2_ring_decode_split", 4),
-                                        ("sp3_ring_weighted_decode_split", 3)])
+                                        ("sp3_ring_weighted_decode_split", 3), ("sp2_ring_eos", 2)])
 def test_llama_sp_multi_gpu_matches_reference_engine(golden_llama, name, world):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -161,6 +163,6 @@ def test_llama_sp_multi_gpu_matches_reference_engine(golden_llama, name, world):
     mask = golden_llama["mask"].astype(bool)
     for logits, tokens, scores in res:
         assert np.abs(logits - golden_llama[f"{name}/logits"])[mask].max() < 1e-10
-        assert tokens == golden_llama[f"{name}/tokens"].tolist()
+        assert tokens == json.loads(str(golden_llama[f"{name}/tokens"]))
         for b in range(len(tokens)):
             assert np.abs(scores[b] - golden_llama[f"{name}/scores{b}"]).max() < 1e-10
