@@ -420,7 +420,7 @@ class LlamaModel:
         return self._layers(ids, self._attn_block(attend, positions))
 
     def _decode_sp_split(self, ids, positions, comm, cache, owner, sp_mode, head_shards, stage, sp_weights):
-        c, d, me = self.config, self.config.head_dim, self.shard.heads
+        d, me = self.config.head_dim, self.shard.heads
         parts = list(sp_weights) if sp_weights else comm.size
         qn, kn = me.q_count * d, me.kv_count * d
         # this rank's query heads (relative to the TP-local heads) and MLP units (relative to the TP-local units)
