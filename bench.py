@@ -580,6 +580,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-ulysses", action="store_true")
+    ap.add_argument("--no-llama", action="store_true", help="skip the config-5 side metric of the default line")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--llama", action="store_true",
                     help="run config 5 instead (LLaMA-3-8B 32K-token prefill with ring SP) and print its line")
@@ -633,6 +634,14 @@ def main():
     del pre["tensors"]
     dec = None if args.no_decode else bench_decode(cea, rank, world, dev)
     uly = None if args.no_ulysses else bench_ulysses(cea, rank, world, dev, args.steps, warmup)
+    llama = None
+    if not args.no_llama:
+        # config 5 as a side metric; a host-side failure here must not lose the main line (every rank takes the
+        # same branch: the leg's collectives are symmetric, so an exception is raised on all ranks alike)
+        try:
+            llama = bench_llama(cea, rank, world, dev, args.steps, warmup)
+        except Exception as exc:  # noqa: BLE001
+            llama = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     status = _lib.device_status(clear=True)
     peak_burst, peak_sus, hbm, peak_kind = _peaks()
     traffic = _traffic_summary()
@@ -682,6 +691,8 @@ def main():
                                           "kernel_ms": a["ms"]}}
     if uly is not None:
         line["ulysses"] = uly
+    if llama is not None:
+        line["llama"] = llama
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
