@@ -140,4 +140,3 @@ def test_assign_tokens_rules():
     with pytest.raises(ValueError):
         assign_tokens(kv, 2, 3, sharded_sizes=[1, 1])
     assert _lib.ABI_VERSION >= 3
-
