@@ -55,8 +55,8 @@ def _peaks():
 
 
 def prefill_kernel_name() -> str:
-    """The tcgen05 prefill kernel libcea.so runs (CEA_PREFILL_KERNEL=1 selects the one-tile kernel)."""
-    return "attn_fwd_tc_kernel" if os.environ.get("CEA_PREFILL_KERNEL", "") == "1" else "attn_fwd_tc2_kernel"
+    """The tcgen05 prefill kernel libcea.so runs."""
+    return "attn_fwd_tc2_kernel"
 
 
 def _traffic_summary():

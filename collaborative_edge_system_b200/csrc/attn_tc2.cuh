@@ -32,9 +32,7 @@
 // complete PV_h(t-1) is complete too, so O_h may be rescaled in place.
 #pragma once
 
-#include <type_traits>
-
-#include "attn_tc.cuh"
+#include "cea_common.cuh"
 
 namespace cea {
 namespace tc2 {
@@ -49,6 +47,11 @@ constexpr int kMmaWarp1 = 11;       // MMA issuer of half 1
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPCol = 64;  // P_h columns within S_h (128 keys x 16 bit = 64 columns)
 constexpr float kRescaleThreshold = 8.0f;
+
+// Instrumentation hook (no code unless a build defines it): CEA_TC2_MARK(half, event, tile).
+#ifndef CEA_TC2_MARK
+#define CEA_TC2_MARK(h, ev, t) ((void)0)
+#endif
 
 template <int D>
 struct Layout {
@@ -77,8 +80,32 @@ struct Layout {
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
+// Operands, strides and tile statistics of one launch (element strides; positions int64).
+struct AttnArgs {
+  const int64_t* q_pos;
+  const int64_t* k_pos;
+  int64_t qpos_sb, qpos_ss, kpos_sb, kpos_ss;
+  void* out;
+  int64_t o_sb, o_ss, o_sh;
+  float* lse;
+  int64_t l_sb, l_sh, l_ss;
+  const int32_t* kv_map;
+  const TileStat* qstat;  // [B][nqt]
+  const TileStat* kstat;  // [B][nkt]
+  const int2* qrange;     // [B][nqt]: first and last key tile each query tile can see
+  int B, Sq, Sk, Hq, Hkv, group, nqt, nkt;
+  float scale_log2;
+  int causal, out_dtype, accumulate;
+};
+
+// warp-uniform bounded wait: every lane waits, the warp continues only if all succeeded
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
+  const bool ok = mbar_wait(bar, parity, abort, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
 struct Params {
-  tc::Params base;
+  AttnArgs base;
   int pair_heads;  // 1: halves are query heads 2p, 2p+1 at one q tile; 0: q tiles 2i, 2i+1 of one head
   int nblk_q;      // CTAs along the query-tile axis
 };
@@ -98,7 +125,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const Params pp) {
   using L = Layout<D>;
-  const tc::Params& p = pp.base;
+  const AttnArgs& p = pp.base;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -246,16 +273,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const bool has_s = kt <= krange.y;  // S_h(j) exists
         // what this pair needs: K(j) for S_h(j), P_h(j-1) and V(j-1) for PV_h(j-1), the other half's turn
         if (has_s && !mbar_wait(bar(L::B_KFULL + j % L::KST), (j / L::KST) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA)) break;
-        if (j > 0 && (!mbar_wait(bar(L::B_PFULL + h), (j - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA) ||
+        // P_h(j-1) and the other issuer's turn are on the critical path and usually short: poll them (a
+        // thread woken from a suspended wait resumes a few hundred cycles after the phase completes)
+        if (j > 0 && (!mbar_spin(bar(L::B_PFULL + h), (j - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA) ||
                       !mbar_wait(bar(L::B_VFULL + (j - 1) % L::VST), ((j - 1) / L::VST) & 1, abort_flag,
                                  CEA_DEV_TIMEOUT_MMA)))
           break;
         if (active1) {
-          const bool turn_ok = h == 0 ? (j == 0 || mbar_wait(bar(L::B_TURN + 1), (j - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA))
-                                      : mbar_wait(bar(L::B_TURN + 0), j & 1, abort_flag, CEA_DEV_TIMEOUT_MMA);
+          const bool turn_ok =
+              h == 0 ? (j == 0 || mbar_spin(bar(L::B_TURN + 1), (j - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_MMA))
+                     : mbar_spin(bar(L::B_TURN + 0), j & 1, abort_flag, CEA_DEV_TIMEOUT_MMA);
           if (!turn_ok) break;
         }
         tc_fence_after();
+        CEA_TC2_MARK(h, 4, j);
         if (j > 0) {
           const int vs = (j - 1) % L::VST;
           const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * L::TILE) >> 4);
@@ -265,6 +296,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     (j > 1 || kk > 0) ? 1u : 0u);
           umma_commit(bar(L::B_PVDONE + h));
           umma_commit(bar(L::B_VEMPTY + vs));
+          CEA_TC2_MARK(h, 6, j);
         }
         if (has_s) {
           const int ks = j % L::KST;
@@ -278,6 +310,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_commit(bar(L::B_SFULL + h));
           umma_commit(bar(L::B_KEMPTY + ks));
         }
+        CEA_TC2_MARK(h, 5, j);
         mbar_arrive(bar(L::B_TURN + h));
         if (!has_s) break;  // that was the last pair
         // next key tile any half can see, from the prefetched statistics
@@ -314,11 +347,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int cls_other = cls_of(h ^ 1, kt);
         if (cls_own == kSkip && cls_other == kSkip) continue;
         const int cls = cls_own == kSkip ? kMasked : cls_own;  // the other half's tile: every key masked here
-        if (!tc::warp_wait(bar(L::B_SFULL + h), it & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
+        CEA_TC2_MARK(h, 3, it);
+        if (!warp_wait(bar(L::B_SFULL + h), it & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        CEA_TC2_MARK(h, 0, it);
         uint32_t s[BN];
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
@@ -362,35 +397,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           m = m_new;
         }
         const float neg_m = (m == -INFINITY) ? 0.f : -m;
-        // P_h = 2^(s*scale - m) as 16-bit pairs into the upper half of S_h (S is in registers)
-        float rs[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) rs[a] = 0.f;
-        auto emit = [&](auto use_poly) {
-#pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float x0 = fmaf(__uint_as_float(s[c * 32 + 2 * e]), p.scale_log2, neg_m);
-              const float x1 = fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), p.scale_log2, neg_m);
-              const float p0 = (decltype(use_poly)::value && ((2 * e) & 7) >= 5) ? exp2_poly3(x0) : fast_exp2(x0);
-              const float p1 =
-                  (decltype(use_poly)::value && ((2 * e + 1) & 7) >= 5) ? exp2_poly3(x1) : fast_exp2(x1);
-              rs[(2 * e) & 7] += p0;
-              rs[(2 * e + 1) & 7] += p1;
-              pk[e] = pack2(p0, p1, kBF16);
-            }
-            tmem_st16(tS + kPCol + c * 16, pk);
-          }
-        };
-        if (CEA_POLY_EXP2 && cls == kFull) {
-          emit(std::true_type{});
-        } else {
-          emit(std::false_type{});
-        }
-        l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
-        // S_h(it) complete => PV_h(it-1) complete: O_h is stable until P_h(it) is released
+        CEA_TC2_MARK(h, 1, it);
+        // S_h(it) complete => PV_h(it-1) complete: O_h is stable until the first chunk of P_h(it) is
+        // released, so a rescale goes first
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
@@ -402,12 +411,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(tO + c * 32, o);
           }
         }
+        // P_h = 2^(s*scale - m) as 16-bit pairs into the upper half of S_h (S is in registers), scaled and
+        // summed with packed pair arithmetic (one instruction per two keys)
+        uint64_t rs2[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) rs2[a] = 0ull;
+        const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t negm2 = f2_pack(neg_m, neg_m);
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c * 32 + 2 * e]), __uint_as_float(s[c * 32 + 2 * e + 1])),
+                             scale2, negm2),
+                      x0, x1);
+            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            rs2[e & 3] = f2_add(rs2[e & 3], f2_pack(p0, p1));
+            pk[e] = pack2(p0, p1, kBF16);
+          }
+          tmem_st16(tS + kPCol + c * 16, pk);
+        }
         tmem_wait_st();
         tc_fence_before();
         // one arrival per warp: 128 per-thread arrivals on one barrier are processed one by one and
         // delayed the MMA issuer by about a thousand cycles per tile
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(L::B_PFULL + h));
+        CEA_TC2_MARK(h, 2, it);
+        {
+          const uint64_t r = f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3]));
+          float r0, r1;
+          f2_unpack(r, r0, r1);
+          l += r0 + r1;
+        }
         ++it;
       }
     }
@@ -416,7 +454,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // PV_h(it-1) is the last product in O_h.  S_h(it-1) completed, hence PV_h(it-2) did: pv_done_h has
     // completed it-1 or it phases, so the parity wait is unambiguous.
     if (ok && it > 0) {
-      ok = tc::warp_wait(bar(L::B_PVDONE + h), (it - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
+      ok = warp_wait(bar(L::B_PVDONE + h), (it - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
       tc_fence_after();
     }
     if (ok && active && !(it == 0 && p.accumulate)) {

@@ -11,7 +11,6 @@
 #include <type_traits>
 
 #include "attn_simt.cuh"
-#include "attn_tc.cuh"
 #include "attn_tc2.cuh"
 #include "cea_common.cuh"
 #include "cea_nccl.cuh"
@@ -199,7 +198,7 @@ DecodePlan decode_plan(const cea_attn_params* p, size_t max_bytes = SIZE_MAX) {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 size_t tc_stats_bytes(const cea_attn_params* p) {
-  const int nqt = (p->Sq + tc::BM - 1) / tc::BM, nkt = (p->Sk + tc::BN - 1) / tc::BN;
+  const int nqt = (p->Sq + tc2::BM - 1) / tc2::BM, nkt = (p->Sk + tc2::BN - 1) / tc2::BN;
   return align256(static_cast<size_t>(p->B) * (nqt + nkt) * sizeof(TileStat)) +
          align256(static_cast<size_t>(p->B) * nqt * sizeof(int2));
 }
@@ -229,33 +228,16 @@ int launch_empty(const cea_attn_params* p, cudaStream_t s) {
   return cuda_check("fill_empty_kernel");
 }
 
-// Which tcgen05 prefill kernel runs: 2 (default) = two query tiles per CTA sharing each K/V tile
-// (attn_tc2.cuh); CEA_PREFILL_KERNEL=1 selects the one-tile kernel (attn_tc.cuh), kept as a
-// reference point for measurements and as a fallback.
-int prefill_version() {
-  static int v = [] {
-    const char* e = getenv("CEA_PREFILL_KERNEL");
-    return (e != nullptr && e[0] == '1') ? 1 : 2;
-  }();
-  return v;
-}
-
-// with an explicit kv_map, heads 2i and 2i+1 must read the same KV head to share a CTA.
-// The map lives on the device, so only the uniform grouping is paired here.
-bool kv_pairs_ok(const cea_attn_params*) { return false; }
-
 int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   const size_t need = tc_stats_bytes(p);
   if (p->workspace == nullptr || p->workspace_bytes < need)
     return fail(CEA_ERR_WORKSPACE, "tcgen05 attention needs %zu workspace bytes, got %zu", need, p->workspace_bytes);
-  const int nqt = (p->Sq + tc::BM - 1) / tc::BM, nkt = (p->Sk + tc::BN - 1) / tc::BN;
+  const int nqt = (p->Sq + tc2::BM - 1) / tc2::BM, nkt = (p->Sk + tc2::BN - 1) / tc2::BN;
   TileStat* qstat = reinterpret_cast<TileStat*>(p->workspace);
   TileStat* kstat = qstat + static_cast<size_t>(p->B) * nqt;
   int2* qrange = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(p->workspace) +
                                          align256(static_cast<size_t>(p->B) * (nqt + nkt) * sizeof(TileStat)));
   {
-    const int warps = p->B * (nqt + nkt);
-    (void)warps;
     const int wq = p->B * nqt, wk = p->B * nkt;
     tile_stats_kernel<<<(wq + 3) / 4, 128, 0, s>>>(p->q_pos, p->qpos_stride[0], p->qpos_stride[1], p->Sq, nqt, p->B,
                                                    0, qstat);
@@ -269,7 +251,7 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
       !make_map(&mk, p->in_dtype, p->k, p->D, p->Sk, p->Hkv, p->B, p->k_stride[1], p->k_stride[2], p->k_stride[0], 128) ||
       !make_map(&mv, p->in_dtype, p->v, p->D, p->Sk, p->Hkv, p->B, p->v_stride[1], p->v_stride[2], p->v_stride[0], 128))
     return fail(CEA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the attention operands");
-  tc::Params tp;
+  tc2::AttnArgs tp;
   tp.q_pos = p->q_pos;
   tp.k_pos = p->k_pos;
   tp.qpos_sb = p->qpos_stride[0];
@@ -300,44 +282,29 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   tp.causal = p->causal;
   tp.out_dtype = p->out_dtype;
   tp.accumulate = p->accumulate;
-  const int64_t grid = static_cast<int64_t>(nqt) * p->Hq * p->B;
-  if (grid > 0x7fffffff) return fail(CEA_ERR_UNSUPPORTED, "grid too large");
   const bool bf = p->in_dtype == CEA_BF16;
-  if (prefill_version() == 2) {
-    // two query tiles per CTA: a GQA head pair when heads pair up on one KV head, else adjacent q tiles
-    tc2::Params pp;
-    pp.base = tp;
-    const bool heads_pair = p->Hq % 2 == 0 && (p->kv_map == nullptr ? (p->Hq / p->Hkv) % 2 == 0 : kv_pairs_ok(p));
-    pp.pair_heads = heads_pair ? 1 : 0;
-    pp.nblk_q = heads_pair ? nqt : (nqt + 1) / 2;
-    const int64_t grid2 = static_cast<int64_t>(pp.nblk_q) * p->B * (heads_pair ? p->Hq / 2 : p->Hq);
+  // two query tiles per CTA: a GQA head pair when the uniform grouping pairs heads on one KV head, else two
+  // adjacent query tiles of one head (an explicit kv_map lives on the device, so it takes the second form)
+  tc2::Params pp;
+  pp.base = tp;
+  const bool heads_pair = p->kv_map == nullptr && p->Hq % 2 == 0 && (p->Hq / p->Hkv) % 2 == 0;
+  pp.pair_heads = heads_pair ? 1 : 0;
+  pp.nblk_q = heads_pair ? nqt : (nqt + 1) / 2;
+  const int64_t grid2 = static_cast<int64_t>(pp.nblk_q) * p->B * (heads_pair ? p->Hq / 2 : p->Hq);
+  if (grid2 > 0x7fffffff) return fail(CEA_ERR_UNSUPPORTED, "grid too large");
 #define CEA_TC2(DD, BF)                                                                                        \
   do {                                                                                                         \
     auto k = tc2::attn_fwd_tc2_kernel<DD, BF>;                                                                 \
     allow_smem(k, tc2::Layout<DD>::SMEM_ALLOC);                                                                \
     k<<<static_cast<unsigned>(grid2), tc2::NUM_THREADS, tc2::Layout<DD>::SMEM_ALLOC, s>>>(mq, mk, mv, pp);     \
   } while (0)
-    if (p->D == 128) {
-      if (bf) CEA_TC2(128, true); else CEA_TC2(128, false);
-    } else {
-      if (bf) CEA_TC2(64, true); else CEA_TC2(64, false);
-    }
-#undef CEA_TC2
-    return cuda_check("attn_fwd_tc2_kernel");
-  }
-#define CEA_TC(DD, BF)                                                                                       \
-  do {                                                                                                       \
-    auto k = tc::attn_fwd_tc_kernel<DD, BF>;                                                                 \
-    allow_smem(k, tc::Layout<DD>::SMEM_ALLOC);                                                               \
-    k<<<static_cast<unsigned>(grid), tc::NUM_THREADS, tc::Layout<DD>::SMEM_ALLOC, s>>>(mq, mk, mv, tp);      \
-  } while (0)
   if (p->D == 128) {
-    if (bf) CEA_TC(128, true); else CEA_TC(128, false);
+    if (bf) CEA_TC2(128, true); else CEA_TC2(128, false);
   } else {
-    if (bf) CEA_TC(64, true); else CEA_TC(64, false);
+    if (bf) CEA_TC2(64, true); else CEA_TC2(64, false);
   }
-#undef CEA_TC
-  return cuda_check("attn_fwd_tc_kernel");
+#undef CEA_TC2
+  return cuda_check("attn_fwd_tc2_kernel");
 }
 
 int launch_decode_plan(const cea_attn_params* p, cudaStream_t s, const DecodePlan& plan, void* workspace);

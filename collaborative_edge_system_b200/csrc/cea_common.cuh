@@ -92,6 +92,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Same contract as mbar_wait, polling with the non-blocking test instead of suspending: a thread woken
+// from mbarrier.try_wait resumes a few hundred cycles after the phase completes, a polling thread within
+// tens.  For a single thread whose wait is on the critical path and short.
+__device__ __forceinline__ bool mbar_spin(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_test(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (global_timer_ns() - t0 > CEA_WAIT_LIMIT_NS) {
+      record_error(code);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+}
+
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -208,21 +227,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^x for x <= 0 on the FMA pipe: x = n + f, n = round(x), f in [-0.5, 0.5];
-// 2^f ~ c0 + f (c1 + f (c2 + f c3)) (least-squares fit, max rel. err 7.5e-5);
-// 2^n applied by adding n to the exponent field.  x is clamped at -125 so the
-// exponent cannot underflow (2^-125 is below anything that matters here).
-__device__ __forceinline__ float exp2_poly3(float x) {
-  const float xc = fmaxf(x, -125.0f);
-  const float t = xc + 12582912.0f;  // 1.5 * 2^23: the integer part lands in the low mantissa bits
-  const float n = t - 12582912.0f;
-  const float f = xc - n;
-  float p = fmaf(0.055171623826026917f, f, 0.2426111251115799f);
-  p = fmaf(p, f, 0.6932609677314758f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic: one instruction issue for two lanes of work).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
 }
-
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 template <typename T> __device__ __forceinline__ float to_f32(T x);
 template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
 template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
