@@ -14,9 +14,12 @@ each appending one token to the last rank's shard - tokens/s and HBM GB/s.
 pinned host memory and the output copied back inside the timed region, every
 step, double-buffered so that the next step's input copies overlap the current
 step's compute.
-``--impl reference`` times the reference algorithm's CPU restatement
-(``oracle/``, numpy + OpenBLAS, all host threads) on a bounded sample of the
-same workload; rank 0 alone runs it.
+``--impl reference`` times the reference's own CPU path (collab_infer, installed
+unmodified under ``baseline/_ref``: its ``ring_attention`` on torch's CPU flash
+kernel, all host threads) on a bounded sample of the same workload; rank 0
+alone runs it.  Without that install it falls back to the numpy restatement in
+``oracle/`` and says so (``kind: "port"``).  ``--cpu-configs`` times the
+reference per benchmark configuration on the host cores.
 """
 
 from __future__ import annotations
@@ -501,41 +504,180 @@ def bench_llama(cea, rank, world, dev, steps, warmup, tp_size=1):
             "weights_gb": model.parameter_bytes() / 1e9}
 
 
-# ----------------------------------------------------------------------------- CPU baseline (oracle)
-def cpu_baseline(seconds_target: float = 15.0):
-    """The reference algorithm's CPU restatement on a bounded sample of the prefill workload.
+# ----------------------------------------------------------------------------- CPU baseline: the reference itself
+REF_ROOT = os.path.join(ROOT, "baseline", "_ref")  # pip install --target of the unmodified reference
 
-    Sample: the last ``nq`` query positions of a causal prefix of ``sk`` tokens,
-    all 32 query heads (GQA 4:1, D=128), fp32 from bf16-rounded inputs; FLOP/s
-    of visible pairs, which converts to the full 131072-token prefill.
-    """
+
+def reference_available() -> bool:
+    """collab_infer (the reference, unmodified) installed under baseline/_ref; put on sys.path."""
+    if not os.path.isdir(os.path.join(REF_ROOT, "collab_infer")):
+        return False
+    if REF_ROOT not in sys.path:
+        sys.path.insert(0, REF_ROOT)
+    os.environ["PYTHONPATH"] = REF_ROOT + os.pathsep + os.environ.get("PYTHONPATH", "")
+    return True
+
+
+def _ref_inputs(S, Hq, Hkv, Dh, batch=1, dtype=torch.bfloat16, seed=0, scale_q=True):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(batch, S, Hq, Dh, generator=g)
+    q = (q / math.sqrt(Dh) if scale_q else q).to(dtype)
+    k = torch.randn(batch, S, Hkv, Dh, generator=g).to(dtype)
+    v = torch.randn(batch, S, Hkv, Dh, generator=g).to(dtype)
+    return q, k, v, torch.arange(S).repeat(batch, 1)
+
+
+def _ref_ring_worker(rank, world, S, Hq, Hkv, Dh, layout, dtype_name, scale_q):
+    """collab_infer's ring_attention (its CPU flash kernel under its own gloo ring) on this rank's shard."""
+    from collab_infer.distributed import ParallelContext
+    from collab_infer.parallel.partition import SequenceLayout
+    from collab_infer.parallel.sequence_parallel import ring_attention
+
+    ctx = ParallelContext(1, world, 1)
+    q, k, v, pos = _ref_inputs(S, Hq, Hkv, Dh, dtype=getattr(torch, dtype_name), scale_q=scale_q)
+    lay = SequenceLayout(S, world, None, layout)
+    ql, kl, vl, pl = (lay.shard(t, rank) for t in (q, k, v, pos))
+    ctx.sp.barrier()
+    t0 = time.perf_counter()
+    ring_attention(ql, kl, vl, pl, pl, ctx.sp, lay.sizes, causal=True, scale=1.0 / math.sqrt(Dh))
+    ctx.sp.barrier()
+    return time.perf_counter() - t0
+
+
+def _ref_ulysses_worker(rank, world, S, H, Dh, batch, weights):
+    from collab_infer.distributed import ParallelContext
+    from collab_infer.parallel.partition import partition_heads, split_sizes
+    from collab_infer.parallel.sequence_parallel import ulysses_attention
+
+    ctx = ParallelContext(1, world, 1)
+    q, k, v, pos = _ref_inputs(S, H, H, Dh, batch=batch, scale_q=False)
+    sizes = split_sizes(S, weights, granularity=128) if weights else split_sizes(S, world)
+    shards = partition_heads(H, H, weights or world)
+    lo = sum(sizes[:rank])
+    sl = slice(lo, lo + sizes[rank])
+    ctx.sp.barrier()
+    t0 = time.perf_counter()
+    ulysses_attention(q[:, sl], k[:, sl], v[:, sl], pos[:, sl], ctx.sp, sizes, shards, causal=True)
+    ctx.sp.barrier()
+    return time.perf_counter() - t0
+
+
+def _ref_decode_worker(rank, world, T, batch, Hq, Hkv, Dh, steps):
+    """collab_infer's distributed_kv_attention of one new token over a head-major bf16 cache shard (its own
+    cache layout, models/cache.py:24,74), ``steps`` steps; seconds per step."""
+    from collab_infer.distributed import ParallelContext
+    from collab_infer.parallel.partition import SequenceLayout
+    from collab_infer.parallel.sequence_parallel import distributed_kv_attention
+
+    ctx = ParallelContext(1, world, 1)
+    lay = SequenceLayout(T, world)
+    n = lay.sizes[rank]
+    g = torch.Generator().manual_seed(rank)
+    kc = torch.randn(batch, Hkv, n, Dh, generator=g).to(torch.bfloat16)
+    vc = torch.randn(batch, Hkv, n, Dh, generator=g).to(torch.bfloat16)
+    kp = lay.shard(torch.arange(T).repeat(batch, 1), rank)
+    q = torch.randn(batch, 1, Hq, Dh, generator=g).to(torch.bfloat16)
+    qp = torch.full((batch, 1), T)
+    ctx.sp.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        distributed_kv_attention(q, kc.transpose(1, 2), vc.transpose(1, 2), qp, kp, ctx.sp, causal=True)
+    ctx.sp.barrier()
+    return (time.perf_counter() - t0) / steps
+
+
+def _ref_launch(fn, world, *args):
+    """Max over ranks of a reference worker under collab_infer's own launch_local (gloo, cores/world threads)."""
+    from collab_infer.distributed import launch_local
+
+    cores = os.cpu_count() or 1
+    if world == 1:
+        torch.set_num_threads(cores)
+        os.environ.update(MASTER_ADDR="127.0.0.1", RANK="0", WORLD_SIZE="1")
+        return fn(0, 1, *args)
+    return max(launch_local(fn, world, args=args, return_results=True, threads_per_rank=max(1, cores // world),
+                            timeout_s=1800))
+
+
+def _port_prefill(nq, sk):
+    """The oracle port (numpy + OpenBLAS): the last nq queries of an sk-token causal prefix; (FLOP, seconds)."""
     import numpy as np
 
     import oracle
 
-    cores = os.cpu_count() or 1
     rng = np.random.default_rng(0)
+    q = (rng.standard_normal((1, nq, HQ, D)) / math.sqrt(D)).astype(np.float32)
+    k = rng.standard_normal((1, sk, HKV, D)).astype(np.float32)
+    v = rng.standard_normal((1, sk, HKV, D)).astype(np.float32)
+    kp = np.arange(sk).reshape(1, sk)
+    qp = kp[:, sk - nq :]
+    t0 = time.perf_counter()
+    oracle.attention_with_lse(q, k, v, qp, kp, True, 1.0 / math.sqrt(D), None, acc=np.float32)
+    return 4.0 * HQ * D * float((qp + 1).sum()), time.perf_counter() - t0
 
-    def run(nq, sk):
-        q = (rng.standard_normal((1, nq, HQ, D)) / math.sqrt(D)).astype(np.float32)
-        k = rng.standard_normal((1, sk, HKV, D)).astype(np.float32)
-        v = rng.standard_normal((1, sk, HKV, D)).astype(np.float32)
-        kp = np.arange(sk).reshape(1, sk)
-        qp = kp[:, sk - nq :]
-        t0 = time.perf_counter()
-        oracle.attention_with_lse(q, k, v, qp, kp, True, 1.0 / math.sqrt(D), None, acc=np.float32)
-        dt = time.perf_counter() - t0
-        pairs = float(((qp + 1).sum()))
-        return 4.0 * HQ * D * pairs, dt
 
-    flops, dt = run(256, 8192)
-    scale = max(1.0, min(64.0, seconds_target / max(dt, 1e-3)))
-    nq = int(min(8192, 256 * scale))
-    nq -= nq % 128
-    flops, dt = run(max(nq, 128), 16384)
-    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-            "sample": f"last {max(nq, 128)} query positions of a 16384-token causal prefix, 32/8 heads, D=128, "
+def cpu_baseline(seconds_target: float = 15.0):
+    """The reference's own CPU path for config 2 on a bounded sample, on this host's cores.
+
+    With the reference installed under baseline/_ref: collab_infer's ring_attention at SP=1 (its
+    attention_with_lse on torch's CPU flash kernel, bf16 inputs computed in fp32, all host threads) over a
+    causal prefix of S tokens with config 2's heads, S sized for about ``seconds_target`` seconds; TFLOP/s of
+    visible pairs.  Without it, the oracle port (numpy) on the last queries of a 16384-token prefix.
+    """
+    cores = os.cpu_count() or 1
+    if reference_available():
+        def run(S):
+            secs = _ref_launch(_ref_ring_worker, 1, S, HQ, HKV, D, "contiguous", "bfloat16", True)
+            return 4.0 * HQ * D * S * (S + 1) / 2, secs
+
+        flops, dt = run(2048)
+        S = int(2048 * math.sqrt(max(1.0, min(256.0, seconds_target / max(dt, 1e-3)))))
+        S = max(2048, min(32768, S - S % 256))
+        flops, dt = run(S)
+        return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "reference", "seconds": dt,
+                "sample": f"collab_infer ring_attention at SP=1 (torch CPU flash, fp32 compute), causal {S}-token "
+                          f"prefix, 32/8 heads, D=128 ({dt:.1f} s)"}
+    flops, dt = _port_prefill(256, 8192)
+    nq = int(min(8192, 256 * max(1.0, min(64.0, seconds_target / max(dt, 1e-3)))))
+    nq = max(128, nq - nq % 128)
+    flops, dt = _port_prefill(nq, 16384)
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port", "seconds": dt,
+            "sample": f"last {nq} query positions of a 16384-token causal prefix, 32/8 heads, D=128, "
                       f"fp32 numpy oracle ({dt:.1f} s)"}
+
+
+def cpu_configs() -> None:
+    """The reference's own CPU/gloo path per benchmark configuration, one JSON line each (host cores only)."""
+    if not reference_available():
+        print(json.dumps({"cpu_configs": "unavailable", "why": "baseline/_ref holds no collab_infer install"}))
+        return
+    cores = os.cpu_count() or 1
+
+    def line(name, value, unit, **kw):
+        print(json.dumps({"cpu_config": name, "value": value, "unit": unit, "cores": cores, "kind": "reference",
+                          **kw}), flush=True)
+
+    f1 = 4.0 * 8 * 64 * 2048 * 2049 / 2
+    for sp in (1, 2):
+        secs = _ref_launch(_ref_ring_worker, sp, 2048, 8, 8, 64, "contiguous", "float32", False)
+        line(f"config1_ring_sp{sp}", f1 / secs / 1e9, "GFLOP/s", ms=secs * 1e3,
+             shape="B1, 8/8 heads, D64, 2048 tokens, causal, fp32")
+    S = 16384
+    f2 = 4.0 * HQ * D * S * (S + 1) / 2
+    for sp in (1, 2, 4, 8):
+        secs = _ref_launch(_ref_ring_worker, sp, S, HQ, HKV, D, "zigzag", "bfloat16", True)
+        line(f"config2_zigzag_ring_sp{sp}", f2 / secs / 1e9, "GFLOP/s", ms=secs * 1e3,
+             shape=f"B1, 32/8 heads, D128, {S} tokens (config 2 at 1/8 length), zigzag, bf16 inputs")
+    S3, w = 8192, [0.4, 0.3, 0.2, 0.1]
+    f3 = 4.0 * UL_B * UL_H * D * S3 * (S3 + 1) / 2
+    secs = _ref_launch(_ref_ulysses_worker, 4, S3, UL_H, D, UL_B, w)
+    line("config3_ulysses_sp4_uneven", f3 / secs / 1e9, "GFLOP/s", ms=secs * 1e3,
+         shape=f"B2, 32/32 heads, D128, {S3} tokens, weights {w}")
+    for sp in (1, 2, 4, 8):
+        secs = _ref_launch(_ref_decode_worker, sp, DEC_T, DEC_B, HQ, HKV, D, 2)
+        line(f"config4_decode_sp{sp}", DEC_B / secs, "tok/s", ms_per_step=secs * 1e3,
+             kv_gbs=2.0 * DEC_B * HKV * DEC_T * D * 2 / secs / 1e9,
+             shape="B16, 32/8 heads, D128, 131072-token bf16 cache, 2 steps")
 
 
 # ----------------------------------------------------------------------------- profiling cases
@@ -585,11 +727,16 @@ def main():
     ap.add_argument("--llama", action="store_true",
                     help="run config 5 instead (LLaMA-3-8B 32K-token prefill with ring SP) and print its line")
     ap.add_argument("--llama-tp", type=int, default=1, help="tensor-parallel size of the --llama run")
+    ap.add_argument("--cpu-configs", action="store_true",
+                    help="time the reference's own CPU/gloo path per configuration (host cores only)")
     ap.add_argument("--ncu-case", choices=["prefill", "decode"], default=None,
                     help="run a small case of one kernel for an ncu capture (no timing, no JSON line)")
     args = ap.parse_args()
     if args.ncu_case:
         ncu_case(args.ncu_case, max(1, args.warmup))
+        return
+    if args.cpu_configs:
+        cpu_configs()
         return
 
     config = {"workload": "zigzag causal ring-attention prefill, LLaMA-3-8B attention shape",
@@ -601,14 +748,23 @@ def main():
         if rank != 0:
             return
         t0 = time.perf_counter()
-        vals = []
-        for _ in range(max(1, args.warmup // 3) + args.steps):
-            vals.append(cpu_baseline(seconds_target=max(2.0, 60.0 / (args.steps + 1))))
-        base = vals[-1]
-        v = statistics.median(x["value"] for x in vals[-args.steps :])
+        # one sample sized so that warm-up plus steps take about two minutes, then `steps` timed samples of it
+        per_step = max(2.0, 120.0 / (args.steps + max(1, args.warmup // 3)))
+        base = cpu_baseline(seconds_target=per_step)
+        samples = [base]
+        if base["kind"] == "reference":
+            S = int(base["sample"].split("causal ")[1].split("-token")[0])
+            flops = 4.0 * HQ * D * S * (S + 1) / 2
+            for _ in range(max(1, args.warmup // 3) + args.steps - 1):
+                secs = _ref_launch(_ref_ring_worker, 1, S, HQ, HKV, D, "contiguous", "bfloat16", True)
+                samples.append({**base, "value": flops / secs / 1e12, "seconds": secs})
+        timed = samples[-args.steps :]
+        v = statistics.median(x["value"] for x in timed)
+        secs = statistics.median(x["seconds"] for x in timed)
         print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
-                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                          "higher_is_better": True, "dtype": "f32", "data": "synthetic", "config": config,
+                          "n_gpus": args.gpus, "steps": len(timed), "warmup": args.warmup,
+                          "ms_per_step": secs * 1e3, "higher_is_better": True, "dtype": "f32",
+                          "data": "synthetic", "config": {**config, "cpu_sample": base["sample"]},
                           "cpu_baseline": {**base, "value": v},
                           "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                           "wall_s": time.perf_counter() - t0}))

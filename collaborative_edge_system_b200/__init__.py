@@ -21,7 +21,7 @@ from .attention import (
     visibility_mask,
 )
 from .cache import KVCache, LayerKVCache, assign_tokens, ring_decode_attention
-from .comm import CommStats, CommWork, Communicator, NetworkConfig, NetworkEmulator, dist_ready
+from .comm import CommStats, CommWork, Communicator, NetworkConfig, NetworkEmulator, adopt, dist_ready
 from .launcher import init_distributed, launch_local
 from .mesh import ParallelContext
 from .partition import HeadShard, SequenceLayout, default_kv_map, offsets_of, partition_heads, split_sizes
@@ -48,6 +48,7 @@ __all__ = [
     "ParallelContext",
     "SequenceLayout",
     "accumulation_dtype",
+    "adopt",
     "assign_tokens",
     "attend_into",
     "attention",

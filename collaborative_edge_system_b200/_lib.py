@@ -20,7 +20,7 @@ F32, F16, BF16, F64 = 0, 1, 2, 3
 _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
 
 CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE, CEA_ERR_NCCL = range(7)
-ABI_VERSION = 5
+ABI_VERSION = 6
 NCCL_ID_BYTES = 128
 MAX_PEERS = 16
 IPC_HANDLE_BYTES = 64
@@ -29,6 +29,7 @@ MAX_SEGMENTS = 64
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
 KIND_NONE, KIND_TC, KIND_DECODE, KIND_SIMT = 0, 1, 2, 3
+DEV_TIMEOUT_PRODUCER, DEV_TIMEOUT_MMA, DEV_TIMEOUT_SOFTMAX, DEV_TIMEOUT_DECODE, DEV_TIMEOUT_PEER = range(0x101, 0x106)
 
 _i64x2 = ctypes.c_int64 * 2
 _i64x3 = ctypes.c_int64 * 3
@@ -64,6 +65,13 @@ class AttnParams(ctypes.Structure):
         ("accumulate", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("new_k", ctypes.c_void_p),
+        ("new_v", ctypes.c_void_p),
+        ("new_pos", ctypes.c_void_p),
+        ("new_k_stride", _i64x3),
+        ("new_v_stride", _i64x3),
+        ("new_pos_stride", _i64x2),
+        ("n_new", ctypes.c_int32),
     ]
 
 
@@ -102,6 +110,8 @@ class PeerMergeParams(ctypes.Structure):
         ("out", ctypes.c_void_p),
         ("o_stride", _i64x3),
         ("out_dtype", ctypes.c_int32),
+        ("fault_flag", ctypes.c_void_p),
+        ("wait_limit_ns", ctypes.c_uint64),
     ]
 
 
@@ -343,8 +353,11 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 
 def attn_params(
-    q, k, v, q_pos, k_pos, out, lse, *, causal: bool, scale: float, kv_map: Optional[torch.Tensor], accumulate: bool
+    q, k, v, q_pos, k_pos, out, lse, *, causal: bool, scale: float, kv_map: Optional[torch.Tensor], accumulate: bool,
+    append=None,
 ) -> AttnParams:
+    """Parameters of one attention call.  ``append = (k_new, v_new, pos_new)``: the last ``k_new.shape[1]``
+    keys are this decode step's new tokens, written into ``k``/``v``/``k_pos`` by the decode kernel."""
     B, Sq, Hq, D = q.shape
     Sk, Hkv = k.shape[1], k.shape[2]
     for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
@@ -369,6 +382,13 @@ def attn_params(
     p.in_dtype = dtype_code(q.dtype)
     p.out_dtype = dtype_code(out.dtype)
     p.accumulate = int(bool(accumulate))
+    if append is not None:
+        nk, nv, npos = append
+        p.new_k, p.new_v, p.new_pos = nk.data_ptr(), nv.data_ptr(), npos.data_ptr()
+        p.new_k_stride = _i64x3(nk.stride(0), nk.stride(1), nk.stride(2))
+        p.new_v_stride = _i64x3(nv.stride(0), nv.stride(1), nv.stride(2))
+        p.new_pos_stride = _i64x2(npos.stride(0), npos.stride(1))
+        p.n_new = nk.shape[1]
     return p
 
 
@@ -457,9 +477,16 @@ def ipc_close(base: int) -> None:
     _check(load().cea_ipc_close(base), "cea_ipc_close")
 
 
-def peer_merge(n: int, rank: int, bufs, flags, epoch: int, W: int, out: torch.Tensor) -> None:
-    """cea_peer_merge: push this rank's slot to every peer, wait for theirs, merge into ``out [B, Sq, H, D]``."""
+def peer_merge(n: int, rank: int, bufs, flags, epoch: int, W: int, out: torch.Tensor, *,
+               fault_flag: Optional[int] = None, wait_limit_ns: int = 0) -> None:
+    """cea_peer_merge: push this rank's slot to every peer, wait for theirs, merge into ``out [B, Sq, H, D]``.
+
+    ``fault_flag`` is a device-visible address (e.g. of pinned host memory) that the kernel sets to
+    ``CEA_DEV_TIMEOUT_PEER`` when its wait for a peer expires; ``wait_limit_ns`` bounds that wait (0: 2 s).
+    """
     p = PeerMergeParams()
+    p.fault_flag = fault_flag
+    p.wait_limit_ns = int(wait_limit_ns)
     p.n, p.rank, p.epoch, p.W = n, rank, epoch, W
     for q in range(n):
         p.bufs[q] = bufs[q]

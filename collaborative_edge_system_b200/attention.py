@@ -143,6 +143,7 @@ def attend_into(
     scale: Optional[float] = None,
     kv_map: KVMap = None,
     accumulate: bool = False,
+    append: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
 ) -> None:
     """Write attention (and lse) into preallocated tensors; ``accumulate`` merges exactly.
 
@@ -150,17 +151,37 @@ def attend_into(
     ``accumulate=True`` the result over these keys is merged into the
     ``(out, lse)`` already stored, which fuses the reference's
     ``merge_attention`` into the kernel epilogue (one ring step).
+
+    ``append = (k_new, v_new, pos_new)`` makes the last ``k_new.shape[1]``
+    keys of ``k``/``v``/``k_pos`` (views of a KV cache) this decode step's new
+    tokens: the split-KV decode kernel writes them into the cache as it reads
+    it, which replaces the separate append launch (``models/cache.py:51-62``).
+    Where another kernel serves the call, the tokens are appended first.
     """
     dev = _lib.require_cuda(q, k, v, out, lse)
     _check_shapes(q, k, v, q_pos, k_pos)
+    if append is not None and (k.dtype != q.dtype or k_pos.dtype != torch.int64 or k_pos.device != dev):
+        _append_tokens(k, v, k_pos, append)  # the kernel would see converted copies, not the cache
+        append = None
     if k.dtype != q.dtype:
         k, v = k.to(q.dtype), v.to(q.dtype)
     scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else float(scale)
     q_pos, k_pos = _positions(q_pos, dev), _positions(k_pos, dev)
     kvm = _kv_map_device(kv_map, q.shape[2], k.shape[2], dev)
     p = _lib.attn_params(q, k, v, q_pos, k_pos, out, lse, causal=causal, scale=scale, kv_map=kvm,
-                         accumulate=accumulate)
+                         accumulate=accumulate, append=append)
+    if append is not None and _lib.kernel_kind(p) != _lib.KIND_DECODE:
+        _append_tokens(k, v, k_pos, append)
+        p = _lib.attn_params(q, k, v, q_pos, k_pos, out, lse, causal=causal, scale=scale, kv_map=kvm,
+                             accumulate=accumulate)
     _lib.attn_fwd(p, dev)
+
+
+def _append_tokens(k: torch.Tensor, v: torch.Tensor, k_pos: torch.Tensor,
+                   append: Tuple[torch.Tensor, torch.Tensor, torch.Tensor]) -> None:
+    """The new tokens into the last rows of the cache views ``k``/``v`` ``[B, T, H, D]`` and ``k_pos``."""
+    nk, nv, npos = append
+    _lib.kv_append(nk, nv, npos, k.transpose(1, 2), v.transpose(1, 2), k_pos, k.shape[1] - nk.shape[1])
 
 
 def attention_with_lse(

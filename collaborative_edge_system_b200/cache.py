@@ -15,8 +15,9 @@ for the ring-mode token placement of ``engine/engine.py:235-244``:
   caches replicated (decode) tokens: the least-loaded one, lowest rank on ties,
   evaluated identically on every rank so no message is needed;
 * :func:`ring_decode_attention` is the ring-mode decode step of the attention
-  layer (``models/llama.py:250-256``): the owner appends, every rank attends to
-  its shard and the partials are merged exactly across the SP group.
+  layer (``models/llama.py:250-256``): the owner's new tokens go into its cache
+  (written by the decode kernel itself while the capacity lasts), every rank
+  attends to its shard and the partials are merged exactly across the SP group.
 """
 
 from __future__ import annotations
@@ -73,12 +74,9 @@ class LayerKVCache:
                          self.pos[:, :n], 0)
         self.k, self.v, self.pos = new_k, new_v, new_pos
 
-    def append(self, k: torch.Tensor, v: torch.Tensor, pos: torch.Tensor) -> None:
-        """Append token-major ``k``/``v`` (``[B, n, H, D]``, any strides with contiguous D) and their positions."""
-        n = k.shape[1]
-        if n == 0:
-            return
+    def _prepare(self, k: torch.Tensor, v: torch.Tensor, pos: torch.Tensor):
         _check_device(k, v)
+        n = k.shape[1]
         if v.shape[:2] != k.shape[:2] or tuple(pos.shape) != (k.shape[0], n):
             raise ValueError(f"k {tuple(k.shape)}, v {tuple(v.shape)} and positions {tuple(pos.shape)} disagree")
         if self.k is not None:
@@ -88,11 +86,32 @@ class LayerKVCache:
             k = k.contiguous()
         if v.stride(3) != 1:
             v = v.contiguous()
-        pos = pos.to(device=k.device, dtype=torch.int64)
+        return k, v, pos.to(device=k.device, dtype=torch.int64)
+
+    def append(self, k: torch.Tensor, v: torch.Tensor, pos: torch.Tensor) -> None:
+        """Append token-major ``k``/``v`` (``[B, n, H, D]``, any strides with contiguous D) and their positions."""
+        n = k.shape[1]
+        if n == 0:
+            return
+        k, v, pos = self._prepare(k, v, pos)
         if self.k is None or self.length + n > self.capacity:
             self._grow(k, v, pos, self.length + n)
         _copy_tokens(self.k, self.v, self.pos, k, v, pos, self.length)
         self.length += n
+
+    def claim(self, k: torch.Tensor, v: torch.Tensor, pos: torch.Tensor):
+        """Reserve the next ``n`` slots for tokens that the attention kernel reading the cache writes itself.
+
+        Returns ``(k, v, pos)`` prepared as :meth:`append` would store them, with
+        the length already advanced (so :meth:`view` includes the slots), or
+        ``None`` when the cache would have to grow: then call :meth:`append`.
+        """
+        n = k.shape[1]
+        if self.k is None or n == 0 or self.length + n > self.capacity:
+            return None
+        k, v, pos = self._prepare(k, v, pos)
+        self.length += n
+        return k, v, pos
 
     def view(
         self, like_k: Optional[torch.Tensor] = None, like_pos: Optional[torch.Tensor] = None
@@ -198,10 +217,15 @@ def ring_decode_attention(
     """
     from .sequence_parallel import distributed_kv_attention
 
+    fused = None
     if decode_owner == comm.rank or comm.size == 1:  # a lone SP rank caches every token (llama.py:225-231)
         if k is None or v is None:
             raise ValueError("the decode owner needs the new tokens' k and v")
-        cache.append(k, v, pos)
+        # within the capacity the decode kernel writes the new tokens into the cache as it reads it (no
+        # separate append launch); growth moves the cache with the append kernel first
+        fused = cache.claim(k, v, pos)
+        if fused is None:
+            cache.append(k, v, pos)
     if k is not None:
         like_k = k
     else:
@@ -210,7 +234,7 @@ def ring_decode_attention(
         like_k = q.new_empty((q.shape[0], 0, num_kv_heads, q.shape[3]))
     kc, vc, pc = cache.view(like_k=like_k, like_pos=pos)
     return distributed_kv_attention(q, kc, vc, pos, pc, comm, causal=causal, scale=scale, kv_map=kv_map,
-                                    kv_block=kv_block)
+                                    kv_block=kv_block, _append=fused)
 
 
 __all__ = ["KVCache", "LayerKVCache", "assign_tokens", "grown_capacity", "ring_decode_attention"]

@@ -630,4 +630,31 @@ class Communicator:
         return CommWork(works, then=landed, not_before=arrive, pin=out)
 
 
-__all__ = ["CommStats", "CommWork", "Communicator", "NetworkConfig", "NetworkEmulator", "dist_ready"]
+def adopt(comm: Any) -> Communicator:
+    """This package's :class:`Communicator` for ``comm``, which may be any communicator with collab_infer's
+    surface (``ranks``, ``group``, ``name``, ``device``, ``stats`` ...).
+
+    collab_infer's ``CollabEngine`` builds its own ``ParallelContext`` and hands
+    its communicators to the attention call sites; those lack the device-lane
+    methods the kernels' orchestration uses (:meth:`Communicator.ring_exchange`,
+    :meth:`Communicator.all_to_all_single`, :meth:`Communicator.all_gather_stacked`).
+    The adopted communicator binds the same process group and rank list, so no
+    group is created, and books its traffic in the caller's ``stats``.  It is
+    built once per foreign communicator and cached on it.
+    """
+    if isinstance(comm, Communicator):
+        return comm
+    mine = getattr(comm, "_cea_adopted", None)
+    if mine is None:
+        mine = Communicator(comm.ranks, comm.group, name=comm.name, device=comm.device, stats=comm.stats,
+                            emulator=getattr(comm, "emulator", None),
+                            small_message_bytes=getattr(comm, "small_message_bytes", None),
+                            comm_dtype=getattr(comm, "comm_dtype", None))
+        try:
+            comm._cea_adopted = mine
+        except AttributeError:  # a communicator that takes no new attributes is adopted on every call
+            pass
+    return mine
+
+
+__all__ = ["CommStats", "CommWork", "Communicator", "NetworkConfig", "NetworkEmulator", "adopt", "dist_ready"]

@@ -119,7 +119,20 @@ int validate(const cea_attn_params* p) {
     return fail(CEA_ERR_INVALID, "null q, out or q_pos");
   if (!empty && p->Sk > 0 && (p->k == nullptr || p->v == nullptr || p->k_pos == nullptr))
     return fail(CEA_ERR_INVALID, "null k, v or k_pos");
+  if (p->n_new < 0 || p->n_new > p->Sk)
+    return fail(CEA_ERR_INVALID, "n_new = %d new tokens do not fit the %d keys", p->n_new, p->Sk);
+  if (p->n_new > 0 && (p->new_k == nullptr || p->new_v == nullptr || p->new_pos == nullptr))
+    return fail(CEA_ERR_INVALID, "null new_k, new_v or new_pos with n_new = %d", p->n_new);
   return CEA_OK;
+}
+
+// the decode kernel copies the new tokens' rows in 16-byte units
+bool append_ok(const cea_attn_params* p) {
+  if (p->n_new == 0) return true;
+  if (!aligned16(p->new_k) || !aligned16(p->new_v)) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((p->new_k_stride[i] % 8) != 0 || (p->new_v_stride[i] % 8) != 0) return false;
+  return true;
 }
 
 enum Kind { kNone = 0, kTc = 1, kDecode = 2, kSimt = 3 };
@@ -131,6 +144,7 @@ bool decode_ok(const cea_attn_params* p) {
   const int G = p->Hq / p->Hkv;
   if (static_cast<int64_t>(p->Sq) * G > dec::MAX_ROWS) return false;
   if ((reinterpret_cast<uintptr_t>(p->q) & 3u) != 0 || (p->q_stride[0] | p->q_stride[1] | p->q_stride[2]) & 1) return false;
+  if (!append_ok(p)) return false;
   return tma_ok(p->k, p->k_stride, p->Sk, p->Hkv, p->B) && tma_ok(p->v, p->v_stride, p->Sk, p->Hkv, p->B);
 }
 
@@ -349,6 +363,28 @@ int launch_decode_plan(const cea_attn_params* p, cudaStream_t s, const DecodePla
   dp.tiles_per_split = plan.tiles_per_split;
   dp.scale_log2 = static_cast<float>(p->scale * 1.4426950408889634);
   dp.causal = p->causal;
+  dp.n_new = p->n_new;
+  dp.new_k = static_cast<const uint16_t*>(p->new_k);
+  dp.new_v = static_cast<const uint16_t*>(p->new_v);
+  dp.nk_sb = p->new_k_stride[0];
+  dp.nk_ss = p->new_k_stride[1];
+  dp.nk_sh = p->new_k_stride[2];
+  dp.nv_sb = p->new_v_stride[0];
+  dp.nv_ss = p->new_v_stride[1];
+  dp.nv_sh = p->new_v_stride[2];
+  dp.new_pos = p->new_pos;
+  dp.np_sb = p->new_pos_stride[0];
+  dp.np_ss = p->new_pos_stride[1];
+  // with an append the key views are the caller's (writable) cache
+  dp.k = const_cast<uint16_t*>(static_cast<const uint16_t*>(p->k));
+  dp.v = const_cast<uint16_t*>(static_cast<const uint16_t*>(p->v));
+  dp.k_sb = p->k_stride[0];
+  dp.k_ss = p->k_stride[1];
+  dp.k_sh = p->k_stride[2];
+  dp.v_sb = p->v_stride[0];
+  dp.v_ss = p->v_stride[1];
+  dp.v_sh = p->v_stride[2];
+  dp.k_pos_out = const_cast<int64_t*>(p->k_pos);
   const dim3 grid(plan.nsplit, p->Hkv, p->B);
 #define CEA_DEC(DD, BF)                                                                              \
   do {                                                                                               \
@@ -490,7 +526,11 @@ int cea_attn_fwd(const cea_attn_params* p, void* stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->Sq == 0 || p->Hq == 0) return CEA_OK;
   if (p->Sk == 0) return p->accumulate ? CEA_OK : launch_empty(p, s);
-  switch (select_kind(p)) {
+  const int kind = select_kind(p);
+  if (p->n_new > 0 && kind != kDecode)
+    return fail(CEA_ERR_UNSUPPORTED, "the fused cache append runs on the split-KV decode path only "
+                                     "(cea_attn_kernel_kind 2); append the tokens separately");
+  switch (kind) {
     case kDecode:
       return launch_decode(p, s);
     case kTc:
@@ -529,9 +569,29 @@ namespace {
 
 constexpr int kNoallocMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+struct NoallocSlot {
+  void* ctx;  // CUDA context the address was looked up in
+  void* ptr;
+};
+NoallocSlot g_noalloc_slot[kNoallocMaxDevices] = {};
 
-// device address of g_noalloc_scratch on the current device (looked up on the first call there)
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+               ? reinterpret_cast<CtxGetCurrentFn>(ptr)
+               : nullptr;
+  }();
+  return fn;
+}
+
+// device address of g_noalloc_scratch in the current context of the current device: looked up on the first
+// call there, and again when the context changed (a device reset makes a new primary context, into which
+// the module and its array are loaded afresh)
 int noalloc_scratch(void** out) {
   int dev = 0;
   const cudaError_t ge = cudaGetDevice(&dev);
@@ -539,16 +599,26 @@ int noalloc_scratch(void** out) {
   if (dev < 0 || dev >= kNoallocMaxDevices)
     return fail(CEA_ERR_UNSUPPORTED, "device %d is beyond the %d devices the decode scratch table covers", dev,
                 kNoallocMaxDevices);
+  const CtxGetCurrentFn get = ctx_get_current_fn();
+  if (get == nullptr) return fail(CEA_ERR_CUDA, "cuCtxGetCurrent is not available from the CUDA driver");
+  auto current = [&]() -> void* {
+    CUcontext c = nullptr;
+    return get(&c) == CUDA_SUCCESS ? static_cast<void*>(c) : nullptr;
+  };
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  NoallocSlot& slot = g_noalloc_slot[dev];
+  void* ctx = current();  // none before the runtime has initialised this device in this process
+  if (ctx == nullptr || slot.ptr == nullptr || slot.ctx != ctx) {
     void* ptr = nullptr;
+    // also makes the device's primary context current when no context is yet (the lookup allocates nothing)
     const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess)
       return fail(CEA_ERR_CUDA, "cudaGetSymbolAddress of the decode scratch on device %d: %s", dev,
                   cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = ptr;
+    slot.ctx = current();
+    slot.ptr = ptr;
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return CEA_OK;
 }
 
@@ -1058,6 +1128,17 @@ int cea_peer_merge(const cea_peer_merge_params* p, void* stream) {
   a.o_sb = p->o_stride[0];
   a.o_ss = p->o_stride[1];
   a.o_sh = p->o_stride[2];
+  a.fault_flag = nullptr;
+  if (p->fault_flag != nullptr) {
+    // the kernel stores into it: accept only memory a kernel can reach (device, managed or pinned host)
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p->fault_flag) != cudaSuccess || attr.devicePointer == nullptr) {
+      cudaGetLastError();
+      return fail(CEA_ERR_INVALID, "cea_peer_merge: fault_flag is not memory a kernel can write");
+    }
+    a.fault_flag = static_cast<int*>(attr.devicePointer);
+  }
+  a.limit_ns = p->wait_limit_ns ? p->wait_limit_ns : static_cast<unsigned long long>(CEA_WAIT_LIMIT_NS);
   const auto s = static_cast<cudaStream_t>(stream);
   if (p->out_dtype == CEA_F32) {
     peer::peer_merge_kernel<float><<<peer::kGrid, peer::kThreads, 0, s>>>(a);

@@ -53,6 +53,18 @@ struct Params {
   int B, Sq, Sk, Hq, Hkv, G, nsplit, tiles_per_split;
   float scale_log2;
   int causal;
+  // decode-step append: the last n_new keys come from new_k / new_v / new_pos and are written into the
+  // cache views (k, v, k_pos_out) by the CTA whose key range holds them, before it reads that range
+  int n_new;
+  const uint16_t* new_k;
+  const uint16_t* new_v;
+  int64_t nk_sb, nk_ss, nk_sh, nv_sb, nv_ss, nv_sh;
+  const int64_t* new_pos;
+  int64_t np_sb, np_ss;
+  uint16_t* k;
+  uint16_t* v;
+  int64_t k_sb, k_ss, k_sh, v_sb, v_ss, v_sh;
+  int64_t* k_pos_out;
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -116,6 +128,30 @@ __global__ void __launch_bounds__(NTHREADS)
     }
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  // decode-step append: this CTA writes the new tokens of its key range for its KV head, and their positions,
+  // into the cache, then orders those generic-proxy stores before its TMA reads of the range
+  const int a0 = p.Sk - p.n_new;  // first new key
+  if (p.n_new > 0 && max(a0, t0 * BKEYS) < k_end) {
+    const int lo = max(a0, t0 * BKEYS);
+    constexpr int CH = D / 8;  // 16-byte chunks of one K or V row
+    const int units = (k_end - lo) * CH;
+    for (int i = threadIdx.x; i < 2 * units; i += NTHREADS) {
+      const bool is_v = i >= units;
+      const int r = is_v ? i - units : i;
+      const int key = lo + r / CH, c = r % CH;
+      const int64_t j = key - a0;
+      const uint16_t* src = is_v ? p.new_v + b * p.nv_sb + j * p.nv_ss + kvh * p.nv_sh
+                                 : p.new_k + b * p.nk_sb + j * p.nk_ss + kvh * p.nk_sh;
+      uint16_t* dst = is_v ? p.v + b * p.v_sb + static_cast<int64_t>(key) * p.v_ss + kvh * p.v_sh
+                           : p.k + b * p.k_sb + static_cast<int64_t>(key) * p.k_ss + kvh * p.k_sh;
+      reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
+    }
+    // every KV head's CTA stores the same positions: this CTA reads its own stores after the barrier below
+    for (int key = lo + threadIdx.x; key < k_end; key += NTHREADS)
+      p.k_pos_out[b * p.kpos_sb + static_cast<int64_t>(key) * p.kpos_ss] =
+          p.new_pos[b * p.np_sb + static_cast<int64_t>(key - a0) * p.np_ss];
+    asm volatile("fence.proxy.async.global;" ::: "memory");
   }
   __syncthreads();
 

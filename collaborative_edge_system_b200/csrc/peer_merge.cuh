@@ -9,6 +9,8 @@
 //   2. after a system-scope fence, adds 1 to its counter in every peer's counter array (one add per CTA),
 //   3. waits, with a bounded spin, until every peer's counter in its own array reaches grid * e, and
 //   4. merges the n slots of every row exactly (log-sum-exp weights), writing the output in the caller's dtype.
+// A wait that runs out (limit_ns) records CEA_DEV_TIMEOUT_PEER (device error word and the optional fault flag)
+// and its CTA writes NaN into the output rows it owns, so a caller never reads stale or partial data.
 // A slot of parity p is rewritten by call e + 2 only after the writer has merged call e + 1, which needed this
 // rank's push of call e + 1, issued after this rank finished merging call e: no call overwrites data a peer
 // may still read.  The grid is small enough to be resident at once on every GPU, so the CTAs waiting in step 3
@@ -32,6 +34,8 @@ struct Args {
   int W, D, B, Sq, H;
   void* out;
   int64_t o_sb, o_ss, o_sh;
+  int* fault_flag;               // optional, device-visible: CEA_DEV_TIMEOUT_PEER after a timeout
+  unsigned long long limit_ns;   // bound of the wait for the peers
 };
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
@@ -69,8 +73,12 @@ __global__ void __launch_bounds__(kThreads) peer_merge_kernel(const Args a) {
       if (q == a.rank) continue;
       uint32_t polls = 0;
       while (ld_acquire_sys(a.flags[a.rank] + q) < a.target) {
-        if ((++polls & 255u) == 0 && global_timer_ns() - t0 > CEA_WAIT_LIMIT_NS) {
+        if ((++polls & 255u) == 0 && global_timer_ns() - t0 > a.limit_ns) {
           record_error(CEA_DEV_TIMEOUT_PEER);
+          if (a.fault_flag != nullptr) {
+            atomicExch_system(a.fault_flag, CEA_DEV_TIMEOUT_PEER);
+            __threadfence_system();
+          }
           give_up = 1;
           break;
         }
@@ -79,11 +87,21 @@ __global__ void __launch_bounds__(kThreads) peer_merge_kernel(const Args a) {
     }
   }
   __syncthreads();
-  if (give_up) return;
-  // ---- 4. exact merge of the n slots, one warp per row
+  // ---- 4. exact merge of the n slots, one warp per row (after a timeout: NaN rows, never stale data)
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const float* mine = a.bufs[a.rank] + static_cast<int64_t>(a.par) * a.n * slot_floats;
+  if (give_up) {
+    for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < a.rows;
+         row += warps) {
+      const int h = row % a.H;
+      const int s = (row / a.H) % a.Sq;
+      const int b = row / (static_cast<int64_t>(a.H) * a.Sq);
+      O* dst = reinterpret_cast<O*>(a.out) + b * a.o_sb + static_cast<int64_t>(s) * a.o_ss + h * a.o_sh;
+      for (int d = lane; d < a.D; d += 32) simt::store_as<O, float>(dst + d, __int_as_float(0x7fc00000));
+    }
+    return;
+  }
   for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < a.rows;
        row += warps) {
     const float li = lane < a.n ? mine[lane * slot_floats + row * a.W + a.D] : -INFINITY;

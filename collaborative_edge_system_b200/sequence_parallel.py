@@ -29,8 +29,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .attention import KVMap, accumulation_dtype, attend_into, attention, attention_with_lse, _merge
-from .comm import Communicator
+from .attention import KVMap, accumulation_dtype, attend_into, attention, _merge
+from .comm import Communicator, adopt
 from .partition import HeadShard, SequenceLayout, offsets_of
 
 TAG_RING_KV = 21
@@ -52,6 +52,7 @@ def shard_sequence(x: torch.Tensor, layout: SequenceLayout, rank: int, dim: int 
 
 def gather_sequence(x_local: torch.Tensor, layout: SequenceLayout, comm: Communicator, dim: int = 1) -> torch.Tensor:
     """All-gather sequence shards in global token order (``sequence_parallel.py:55-62``)."""
+    comm = adopt(comm)
     if comm.size == 1:
         return x_local
     return layout.unshard(comm.all_gather_list(x_local, dim=dim, sizes=layout.sizes), dim=dim)
@@ -82,12 +83,16 @@ def ring_attention(
     with ``return_lse=True`` also the ``[B, Hq, s_i]`` log-sum-exp over all
     keys (accumulation dtype), which the reference computes but drops.
     """
+    comm = adopt(comm)
     n, r = comm.size, comm.rank
     if n == 1:
-        out, lse = attention_with_lse(q, k, v, q_pos, k_pos, causal=causal, scale=scale, kv_map=kv_map,
-                                      kv_block=kv_block)
-        res = out.to(q.dtype)
-        return (res, lse) if return_lse else res
+        # the kernel writes q.dtype directly (no accumulation-dtype output and cast pass)
+        if not return_lse:
+            return attention(q, k, v, q_pos, k_pos, causal=causal, scale=scale, kv_map=kv_map, kv_block=kv_block)
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        lse = torch.empty(q.shape[0], q.shape[2], q.shape[1], dtype=accumulation_dtype(q.dtype), device=q.device)
+        attend_into(q, k, v, q_pos, k_pos, out, lse, causal=causal, scale=scale, kv_map=kv_map)
+        return out, lse
     if len(kv_sizes) != n or kv_sizes[r] != k.shape[1]:
         raise ValueError(f"kv_sizes {list(kv_sizes)} inconsistent with local block of {k.shape[1]} tokens")
     B, Sq, Hq, D = q.shape
@@ -160,6 +165,7 @@ def ulysses_scatter(
     Returns ``(q, k, v, positions)`` over the full sequence (rank order);
     q/k/v are views of one received buffer.
     """
+    comm = adopt(comm)
     n, r = comm.size, comm.rank
     B, s_local, _, D = q.shape
     _check_ulysses(comm, seq_sizes, head_shards, s_local)
@@ -199,6 +205,7 @@ def ulysses_gather(
     out_heads: torch.Tensor, comm: Communicator, seq_sizes: Sequence[int], head_shards: Sequence[HeadShard]
 ) -> torch.Tensor:
     """Head-sharded ``[B, S, h_i, D]`` -> ``[B, s_i, H, D]`` (``sequence_parallel.py:182-194``)."""
+    comm = adopt(comm)
     n, r = comm.size, comm.rank
     B, S, h_r, D = out_heads.shape
     starts = offsets_of(seq_sizes)
@@ -247,6 +254,7 @@ def ulysses_attention(
     Returns ``(out [B, s_i, Hq, D], (k_heads, v_heads, pos_full))``; the second
     element holds this rank's KV heads over the new tokens, for a head-sharded cache.
     """
+    comm = adopt(comm)
     me = head_shards[comm.rank]
     q_f, k_f, v_f, pos_f = ulysses_scatter(q, k, v, positions, comm, seq_sizes, head_shards)
     k_att, v_att, p_att = k_f, v_f, pos_f
@@ -261,7 +269,7 @@ def ulysses_attention(
 
 def gather_heads(out_local: torch.Tensor, comm: Communicator, head_shards: Sequence[HeadShard]) -> torch.Tensor:
     """All-gather per-rank head slices ``[B, S, h_i, D]`` into ``[B, S, H, D]`` (``:242-244``)."""
-    return comm.all_gather(out_local, dim=2, sizes=[sh.q_count for sh in head_shards])
+    return adopt(comm).all_gather(out_local, dim=2, sizes=[sh.q_count for sh in head_shards])
 
 
 # ----------------------------------------------------------------------------
@@ -279,18 +287,23 @@ def distributed_kv_attention(
     scale: Optional[float] = None,
     kv_map: KVMap = None,
     kv_block: Optional[int] = None,
+    _append: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
 ) -> torch.Tensor:
     """Replicated queries against a sequence-sharded cache (``sequence_parallel.py:250-280``).
 
     Each rank attends over its shard (split-KV decode kernel), writing its
     partial straight into a packed ``[B, Sq, H, D+4]`` message (out, lse,
     padding); one all-gather of the messages and an exact n-way merge over
-    the gathered buffer follow.
+    the gathered buffer follow.  ``_append`` (this package's KV cache only) hands the decode step's new
+    tokens to the decode kernel, which writes them into the last rows of ``k_local``/``v_local``/
+    ``k_pos_local`` as it reads them.
     """
+    comm = adopt(comm)
     if comm.size == 1:
-        o, _ = attention_with_lse(q, k_local, v_local, q_pos, k_pos_local, causal=causal, scale=scale,
-                                  kv_map=kv_map, kv_block=kv_block)
-        return o.to(q.dtype)
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        attend_into(q, k_local, v_local, q_pos, k_pos_local, out, None, causal=causal, scale=scale, kv_map=kv_map,
+                    append=_append)
+        return out
     # the local partial goes straight into the packed [B, Sq, H, D+4] message: out in [0, D), lse at D, rows
     # padded to 16 bytes so the kernels keep their vector stores
     B, Sq, Hq, D = q.shape
@@ -300,32 +313,52 @@ def distributed_kv_attention(
         # one node, peers mapped: the partial goes into this rank's slot of its own receive buffer, and one
         # kernel pushes it to every peer, waits for theirs and merges (no NCCL call)
         pd.epoch += 1
-        slot = pd.slot(pd.epoch & 1, comm.rank).view(B, Sq, Hq, W)
+        slot = pd.slot(pd.epoch & 1, comm.rank, B * Sq * Hq * W).view(B, Sq, Hq, W)
         attend_into(q, k_local, v_local, q_pos, k_pos_local, slot[..., :D], slot[..., D].permute(0, 2, 1),
-                    causal=causal, scale=scale, kv_map=kv_map)
+                    causal=causal, scale=scale, kv_map=kv_map, append=_append)
         out = torch.empty(B, Sq, Hq, D, dtype=q.dtype, device=q.device)
-        _lib.peer_merge(comm.size, comm.rank, pd.bufs, pd.flags, pd.epoch, W, out)
+        _lib.peer_merge(comm.size, comm.rank, pd.bufs, pd.flags, pd.epoch, W, out, fault_flag=pd.fault.data_ptr(),
+                        wait_limit_ns=_peer_wait_limit_ns())
         comm.stats.record(f"{comm.name}.all_gather", slot.numel() * 4 * (comm.size - 1), 0.0)
+        comm.stats.record(f"{comm.name}.peer_merge", 0, 0.0)
         return out
     packed = torch.empty(B, Sq, Hq, D + 4, dtype=accumulation_dtype(q.dtype), device=q.device)
     attend_into(q, k_local, v_local, q_pos, k_pos_local, packed[..., :D], packed[..., D].permute(0, 2, 1),
-                causal=causal, scale=scale, kv_map=kv_map)
+                causal=causal, scale=scale, kv_map=kv_map, append=_append)
     return _merge_stacked(comm.all_gather_stacked(packed), D, q.dtype)
+
+
+PEER_WAIT_ENV = "CEA_PEER_WAIT_MS"
+
+
+def _peer_wait_limit_ns() -> int:
+    """Bound of the peer-memory decode exchange's wait for the other ranks, from ``$CEA_PEER_WAIT_MS``
+    (0, the default, keeps the kernels' built-in 2 s)."""
+    return int(float(os.environ.get(PEER_WAIT_ENV, "0")) * 1e6)
+
+
+class PeerExchangeTimeout(RuntimeError):
+    """A rank's peer-memory decode exchange gave up waiting for another rank's partial (CEA_DEV_TIMEOUT_PEER)."""
 
 
 class _PeerDecode:
     """Receive slots and counters of the peer-memory decode merge for one communicator.
 
-    One device allocation per rank holds 2 parities x n ranks x ``slot_floats`` floats followed by n uint64
-    counters (zeroed); every rank maps every peer's allocation (CUDA IPC).  Built collectively on the first
-    multi-rank decode call: if any rank cannot map its peers (no peer access, ranks on several nodes), all
-    ranks agree to keep the all-gather path.
+    One device allocation per rank holds 2 parities x n ranks x ``capacity`` floats followed by n uint64
+    counters (zeroed); every rank maps every peer's allocation (CUDA IPC).  A call of ``slot_floats <=
+    capacity`` floats per slot uses the first ``2 * n * slot_floats`` of the data region (the kernel derives
+    the slot offsets from the call's own size).  Built collectively on the first multi-rank decode call, and
+    rebuilt collectively when a call needs larger slots (every rank sees the same shapes); if any rank
+    cannot map its peers (no peer access, ranks on several nodes), all ranks keep the all-gather path.
+    ``fault`` is a pinned host word the kernel sets when its wait for a peer runs out; the host reads it
+    without synchronising.
     """
 
-    def __init__(self, comm: Communicator, slot_floats: int, device: torch.device):
+    def __init__(self, comm: Communicator, capacity: int, device: torch.device):
         n, r = comm.size, comm.rank
-        self.slot_floats, self.epoch, self.bases = slot_floats, 0, []
-        data = 2 * n * slot_floats
+        self.capacity, self.epoch, self.bases = capacity, 0, []
+        self.fault = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        data = 2 * n * capacity
         self.mem = torch.zeros(data + 2 * n, dtype=torch.float32, device=device)  # counters after the slots
         torch.cuda.synchronize(device)  # zeroed before any peer can add to the counters
         try:
@@ -355,9 +388,9 @@ class _PeerDecode:
         if not self.ok:
             self.close()
 
-    def slot(self, par: int, rank: int) -> torch.Tensor:
+    def slot(self, par: int, rank: int, slot_floats: int) -> torch.Tensor:
         n = len(self.bufs)
-        return self.mem[: 2 * n * self.slot_floats].view(2, n, self.slot_floats)[par, rank]
+        return self.mem[: 2 * n * slot_floats].view(2, n, slot_floats)[par, rank]
 
     def close(self) -> None:
         for base in self.bases:
@@ -367,15 +400,38 @@ class _PeerDecode:
 
 def _peer_decode(comm: Communicator, slot_floats: int, q: torch.Tensor) -> Optional[_PeerDecode]:
     """The communicator's peer-memory decode exchange, if it applies to this call (the same decision on every
-    rank: it depends only on the communicator, the environment and the shapes)."""
+    rank: it depends only on the communicator, the environment, the shapes and the exchange's own history).
+
+    Raises :class:`PeerExchangeTimeout` once when an earlier call's exchange timed out on this rank; the
+    communicator then uses the all-gather path.
+    """
     if (os.environ.get("CEA_PEER_DECODE", "1") == "0" or not comm.on_device or comm.size > _lib.MAX_PEERS
             or not q.is_cuda or accumulation_dtype(q.dtype) != torch.float32):
         return None
+    if getattr(comm, "_cea_peer_failed", False):
+        return None
     pd = getattr(comm, "_cea_peer_decode", None)
+    if pd is not None and int(pd.fault[0]) != 0:
+        # the peers' call numbering no longer agrees with this rank's: never touch these buffers again (the
+        # allocation stays alive, a late peer may still store into it)
+        comm._cea_peer_failed = True
+        pd.close()
+        comm._cea_peer_retired = [pd]
+        raise PeerExchangeTimeout(
+            f"{comm.name}: the distributed-KV decode exchange gave up waiting for a peer's partial "
+            f"(device status CEA_DEV_TIMEOUT_PEER); this communicator now uses the all-gather path")
+    if pd is not None and pd.ok and slot_floats > pd.capacity:
+        # larger slots: every rank rebuilds (same shapes everywhere); no kernel of any rank may still use the
+        # old buffers when they are released
+        torch.cuda.synchronize(q.device)
+        dist.barrier(group=comm.group)
+        pd.close()
+        dist.barrier(group=comm.group)
+        pd = None
     if pd is None:
         pd = _PeerDecode(comm, slot_floats, q.device)
         comm._cea_peer_decode = pd
-    return pd if pd.ok and pd.slot_floats == slot_floats else None
+    return pd if pd.ok else None
 
 
 def _merge_stacked(parts: torch.Tensor, D: int, out_dtype: torch.dtype) -> torch.Tensor:
@@ -390,6 +446,7 @@ def _merge_stacked(parts: torch.Tensor, D: int, out_dtype: torch.dtype) -> torch
 
 
 __all__ = [
+    "PeerExchangeTimeout",
     "distributed_kv_attention",
     "gather_heads",
     "gather_sequence",

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define CEA_ABI_VERSION 5
+#define CEA_ABI_VERSION 6
 
 enum cea_status {
   CEA_OK = 0,
@@ -90,6 +90,20 @@ typedef struct cea_attn_params {
   int32_t accumulate;
   void* workspace;
   size_t workspace_bytes;
+  /* Optional decode-step cache append, served by the split-KV decode path only (cea_attn_kernel_kind 2;
+   * other paths fail with CEA_ERR_UNSUPPORTED).  The last n_new of the Sk keys are this step's new
+   * tokens: the kernel reads their K, V and positions from new_k / new_v ([B, n_new, Hkv, D], element
+   * strides b, s, h; D contiguous, rows 16-byte aligned) and new_pos ([B, n_new]) and writes them into the
+   * last n_new rows of k, v and k_pos, which must therefore be writable (the caller's KV-cache views).
+   * This replaces the separate append launch before the decode (collab_infer models/cache.py:51-62,
+   * engine/engine.py:239-243).  n_new = 0 (zero-initialised) disables it. */
+  const void* new_k;
+  const void* new_v;
+  const int64_t* new_pos;
+  int64_t new_k_stride[3];
+  int64_t new_v_stride[3];
+  int64_t new_pos_stride[2];
+  int32_t n_new;
 } cea_attn_params;
 
 /* Bytes of workspace cea_attn_fwd needs for these parameters (0 if none). */
@@ -123,10 +137,15 @@ int cea_decode_splitkv(const cea_attn_params* p, void* stream);
  *
  * The first call on a device looks the array's device address up
  * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture.  Calls share the array, so calls that overlap on
+ * before any stream capture.  The address is kept per device and looked up
+ * again when the device's current CUDA context changes (after a device reset
+ * the module, and the array with it, is loaded into a new context); the array's
+ * contents do not survive that.  Calls share the array, so calls that overlap on
  * the GPU (for example on two streams) race and must be ordered by the caller.
- * The split count is reduced to fit the array.  A call whose single split of
- * partials, B*Hq*Sq*(D+1)*4 bytes, exceeds it fails with CEA_ERR_WORKSPACE.
+ * The split count is reduced to fit the array (e.g. B=128, Hq=16, D=128,
+ * Sq=1: 1.06 MB per split, at most 7 splits where the regular plan may use
+ * more).  A call whose single split of partials, B*Hq*Sq*(D+1)*4 bytes,
+ * exceeds it fails with CEA_ERR_WORKSPACE.
  * It never calls cudaMalloc or cudaFree.
  */
 #define CEA_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -358,7 +377,13 @@ int cea_allgather(cea_nccl_comm* comm, const void* send, void* recv, size_t byte
  * calls cea_peer_merge, which stores that slot into every peer's buffer,
  * signals every peer through its counters, waits (bounded) for every peer's
  * data and writes the merged [B, Sq, H, D] output.  Every rank must make the
- * same sequence of calls; a wait that expires records CEA_DEV_TIMEOUT_PEER.
+ * same sequence of calls.  A wait that expires (after wait_limit_ns, or the
+ * built-in 2 s when it is 0) records CEA_DEV_TIMEOUT_PEER in the device error
+ * word and, when fault_flag is set, in *fault_flag (a store the host can read
+ * without synchronising when it points to mapped pinned host memory), and the
+ * rows the timed-out CTAs own are written as NaN.  After a timeout the
+ * buffers' call numbering is no longer shared by the ranks: do not call again
+ * on them.
  */
 #define CEA_MAX_PEERS 16
 typedef struct cea_peer_merge_params {
@@ -370,6 +395,8 @@ typedef struct cea_peer_merge_params {
   void* out;
   int64_t o_stride[3]; /* b, s, h */
   int32_t out_dtype;   /* F32, BF16 or F16 */
+  int32_t* fault_flag;    /* optional: set to CEA_DEV_TIMEOUT_PEER on a timeout (device-visible address) */
+  uint64_t wait_limit_ns; /* bound of the wait for the peers; 0 = the built-in 2 s */
 } cea_peer_merge_params;
 
 int cea_peer_merge(const cea_peer_merge_params* p, void* stream);

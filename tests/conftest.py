@@ -9,6 +9,8 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
+if GOLDEN not in sys.path:  # the fixture generators also define how some inputs are regenerated
+    sys.path.insert(0, GOLDEN)
 
 
 def pytest_configure(config):
@@ -56,4 +58,10 @@ def golden_wire():
 @pytest.fixture(scope="session")
 def golden_llama():
     data = np.load(os.path.join(GOLDEN, "llama_sp.npz"), allow_pickle=False)
+    return {k: data[k] for k in data.files}
+
+
+@pytest.fixture(scope="session")
+def golden_config1():
+    data = np.load(os.path.join(GOLDEN, "config1.npz"), allow_pickle=False)
     return {k: data[k] for k in data.files}

@@ -28,7 +28,11 @@ def install_oracle_compute():
     def npy(t):
         return t.detach().cpu().numpy()
 
-    def attend_into(q, k, v, q_pos, k_pos, out, lse, *, causal=True, scale=None, kv_map=None, accumulate=False):
+    def attend_into(q, k, v, q_pos, k_pos, out, lse, *, causal=True, scale=None, kv_map=None, accumulate=False,
+                    append=None):
+        if append is not None:  # the new tokens into the last rows of the cache views
+            n = append[0].shape[1]
+            k[:, -n:], v[:, -n:], k_pos[:, -n:] = append
         o, l = oracle.attention_with_lse(npy(q), npy(k), npy(v), npy(q_pos), npy(k_pos), causal, scale, kv_list(kv_map))
         if accumulate:
             o, l = oracle.merge_attention(npy(out).astype(np.float64), npy(lse).astype(np.float64), o, l)
@@ -181,8 +185,20 @@ def golden_inputs():
     return {k: torch.from_numpy(data[f"sp/{k}"]) for k in ("q", "k", "v", "pos")}
 
 
-def sp_worker(rank, world, kind, weights, causal):
-    """Ring, Ulysses and distributed-KV decode over gloo with the reference's SP test inputs."""
+def _reference_context(world, ref_root):
+    """collab_infer's own ParallelContext (what CollabEngine builds), imported from the reference tree."""
+    import sys
+
+    if ref_root not in sys.path:
+        sys.path.insert(0, ref_root)
+    from collab_infer.distributed import ParallelContext as ReferenceContext
+
+    return ReferenceContext(1, world, 1)
+
+
+def sp_worker(rank, world, kind, weights, causal, ref_root=None):
+    """Ring, Ulysses and distributed-KV decode over gloo with the reference's SP test inputs; with ``ref_root``
+    the functions get the reference's own communicator instead of this package's."""
     install_oracle_compute()
     from collaborative_edge_system_b200 import ParallelContext, SequenceLayout, partition_heads
     from collaborative_edge_system_b200.sequence_parallel import (
@@ -191,7 +207,7 @@ def sp_worker(rank, world, kind, weights, causal):
         ulysses_attention,
     )
 
-    ctx = ParallelContext(1, world, 1)
+    ctx = _reference_context(world, ref_root) if ref_root else ParallelContext(1, world, 1)
     t = golden_inputs()
     q, k, v, pos = t["q"], t["k"], t["v"], t["pos"]
     S, HQ, HKV = q.shape[1], q.shape[2], k.shape[2]

@@ -76,6 +76,60 @@ def decode_worker(rank, world, T, B, Hq, Hkv, D):
     return float(np.abs(_np(out) - ref).max()), str(out.dtype)
 
 
+def ref_surface_worker(rank, world):
+    """Ring (zigzag, GQA, uneven weights), Ulysses (uneven heads and tokens) and distributed-KV decode given a
+    communicator with nothing beyond collab_infer's Communicator surface, as CollabEngine passes it."""
+    import collaborative_edge_system_b200 as cea
+    from ref_surface import ReferenceSurfaceComm
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    comm = ReferenceSurfaceComm(ctx.sp)
+    assert not hasattr(comm, "ring_exchange") and not hasattr(comm, "on_device")
+    g = torch.Generator().manual_seed(11)
+    res = {}
+    # ring
+    S, Hq, Hkv, D = 1024, 8, 2, 128
+    q = torch.randn(1, S, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, S, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, S, Hkv, D, generator=g).to(torch.bfloat16)
+    pos = torch.arange(S).view(1, S)
+    lay = cea.SequenceLayout(S, world, [2, 1] if world == 2 else None, "zigzag")
+    ql, kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (q, k, v, pos))
+    out, lse = cea.ring_attention(ql, kl, vl, pl, pl, comm, lay.sizes, causal=True, return_lse=True)
+    ref_o, ref_l = oracle.attention_with_lse(_np(q), _np(k), _np(v), pos.numpy(), pos.numpy(), True)
+    idx = lay.indices(rank).numpy()
+    res["ring_out"] = float(np.abs(_np(out) - ref_o[:, idx]).max())
+    res["ring_lse"] = float(np.abs(_np(lse) - ref_l[:, :, idx]).max())
+    # Ulysses
+    S, Hq, Hkv = 512, 8, 8
+    q = torch.randn(2, S, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(2, S, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(2, S, Hkv, D, generator=g).to(torch.bfloat16)
+    pos = torch.arange(S).repeat(2, 1)
+    w = [3, 1] if world == 2 else None
+    lay = cea.SequenceLayout(S, world, w, "contiguous")
+    shards = cea.partition_heads(Hq, Hkv, w or world)
+    ql, kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (q, k, v, pos))
+    out, _ = cea.ulysses_attention(ql, kl, vl, pl, comm, lay.sizes, shards)
+    ref = oracle.attention(_np(q), _np(k), _np(v), pos.numpy(), pos.numpy(), True)
+    res["ulysses"] = float(np.abs(_np(out) - ref[:, lay.indices(rank).numpy()]).max())
+    # distributed-KV decode
+    T, B, Hq, Hkv = 3000, 4, 8, 2
+    q = torch.randn(B, 1, Hq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+    kp = torch.arange(T).repeat(B, 1)
+    qp = torch.full((B, 1), T)
+    lay = cea.SequenceLayout(T, world)
+    kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (k, v, kp))
+    out = cea.distributed_kv_attention(q.to(dev), kl, vl, qp.to(dev), pl, comm)
+    ref = oracle.attention(_np(q), _np(k), _np(v), qp.numpy(), kp.numpy(), True)
+    res["decode"] = float(np.abs(_np(out) - ref).max())
+    res["stats"] = ctx.stats.as_dict()
+    return res
+
+
 def nccl_abi_worker(rank, world):
     """libcea.so's own NCCL communicator: ring step, uneven all-to-all and all-gather between the GPUs."""
     import ctypes
@@ -246,3 +300,142 @@ def llama_worker(rank, world, gold, name):
     tokens, scores = generate_greedy(model, prompts, int(gold["new_tokens"]), ctx.sp, return_scores=True,
                                      sp_decode_split=pc.get("sp_decode_split", False), stage=ctx.stage, **gen, **kw)
     return logits.cpu().numpy(), tokens, [sc.cpu().numpy() for sc in scores]
+
+
+def _sample_rows(n, count):
+    """``count`` local query rows spread over ``[0, n)`` (first and last included)."""
+    return np.unique(np.linspace(0, n - 1, num=min(n, count)).round().astype(np.int64))
+
+
+def config1_ring_worker(rank, world):
+    """Config 1 at its shape: fp32 ring attention (contiguous, 1024 tokens per rank at SP=2) with its LSE."""
+    import collaborative_edge_system_b200 as cea
+    from make_golden_config1 import config1_inputs
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    q, k, v, pos = config1_inputs()
+    lay = cea.SequenceLayout(q.shape[1], world)
+    ql, kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (q, k, v, pos))
+    out, lse = cea.ring_attention(ql, kl, vl, pl, pl, ctx.sp, lay.sizes, causal=True, return_lse=True)
+    return out.cpu().numpy(), lse.cpu().numpy(), lay.indices(rank).numpy(), str(out.dtype)
+
+
+def config2_ring_worker(rank, world, S, rows):
+    """Config 2 at a reduced sequence: zigzag causal GQA ring (32 query / 8 KV heads, head_dim 128, bf16, q
+    scaled by 1/sqrt(128)), output and LSE of ``rows`` sampled local query rows against the oracle over all
+    keys."""
+    import collaborative_edge_system_b200 as cea
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    g = torch.Generator().manual_seed(2024)
+    Hq, Hkv, D = 32, 8, 128
+    q = (torch.randn(1, S, Hq, D, generator=g) / np.sqrt(D)).to(torch.bfloat16)
+    k = torch.randn(1, S, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, S, Hkv, D, generator=g).to(torch.bfloat16)
+    pos = torch.arange(S).view(1, S)
+    lay = cea.SequenceLayout(S, world, None, "zigzag")
+    ql, kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (q, k, v, pos))
+    out, lse = cea.ring_attention(ql, kl, vl, pl, pl, ctx.sp, lay.sizes, causal=True,
+                                  scale=1.0 / np.sqrt(D), return_lse=True)
+    local = _sample_rows(lay.sizes[rank], rows)
+    glob = lay.indices(rank).numpy()[local]
+    ref_o, ref_l = oracle.attention_with_lse(_np(q[:, glob]), _np(k), _np(v), pos.numpy()[:, glob], pos.numpy(),
+                                             True, 1.0 / np.sqrt(D))
+    eo = float(np.abs(_np(out[:, local]) - ref_o).max())
+    el = float(np.abs(_np(lse[:, :, local]) - ref_l).max())
+    return eo, el, str(out.dtype), ctx.stats.as_dict()
+
+
+def config3_ulysses_worker(rank, world, S, weights, rows):
+    """Config 3 at a reduced sequence: Ulysses MHA (32 heads, head_dim 128, batch 2, bf16, causal) with uneven
+    capability weights: token shares split on a 128-token granularity, heads by the engine's partition."""
+    import collaborative_edge_system_b200 as cea
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    g = torch.Generator().manual_seed(2025)
+    B, H, D = 2, 32, 128
+    q = torch.randn(B, S, H, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, S, H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, H, D, generator=g).to(torch.bfloat16)
+    pos = torch.arange(S).repeat(B, 1)
+    sizes = cea.split_sizes(S, weights, granularity=128)
+    shards = cea.partition_heads(H, H, weights)
+    start = sum(sizes[:rank])
+    sl = slice(start, start + sizes[rank])
+    out, (kh, vh, ph) = cea.ulysses_attention(*(t[:, sl].to(dev) for t in (q, k, v, pos)), ctx.sp, sizes, shards)
+    local = _sample_rows(sizes[rank], rows)
+    glob = start + local
+    ref = oracle.attention(_np(q[:, glob]), _np(k), _np(v), pos.numpy()[:, glob], pos.numpy(), True)
+    me = shards[rank]
+    ek = float(np.abs(_np(kh) - _np(k[:, :, me.kv_start : me.kv_start + me.kv_count])).max())
+    return float(np.abs(_np(out[:, local]) - ref).max()), ek, sizes, [sh.q_count for sh in shards]
+
+
+def peer_timeout_worker(rank, world, wait_ms):
+    """Failure detection on the peer-memory decode exchange, made on the host: the last rank skips one decode
+    call.  The other ranks' exchange waits run out after ``wait_ms`` (a limit set at run time for that call
+    only) and must come back cleanly: output rows NaN (never stale data), the pinned fault word and the device
+    error word set to CEA_DEV_TIMEOUT_PEER, the context still usable; their next call raises
+    PeerExchangeTimeout once and later calls take the all-gather path.  The skipping rank waits at a host
+    barrier, with no kernel in flight, until the others have given up, so its buffers stay mapped meanwhile."""
+    import os
+    import time
+
+    import torch.distributed as dist
+
+    import collaborative_edge_system_b200 as cea
+    from collaborative_edge_system_b200 import _lib
+    from collaborative_edge_system_b200.sequence_parallel import PeerExchangeTimeout
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = cea.ParallelContext(1, world, 1, device=dev)
+    T, B, Hq, Hkv, D = 2048, 2, 8, 2, 128
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(B, 1, Hq, D, generator=g).to(torch.bfloat16).to(dev)
+    k = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16)
+    kp = torch.arange(T).repeat(B, 1)
+    qp = torch.full((B, 1), T, device=dev)
+    lay = cea.SequenceLayout(T, world)
+    kl, vl, pl = (lay.shard(t, rank).to(dev) for t in (k, v, kp))
+    args = (q, kl, vl, qp, pl, ctx.sp)
+    res = {}
+    # every kernel of the path loaded once, then one exchange that every rank joins (built-in wait limit)
+    os.environ["CEA_PEER_DECODE"] = "0"
+    want = cea.distributed_kv_attention(*args)
+    os.environ["CEA_PEER_DECODE"] = "1"
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    first = cea.distributed_kv_attention(*args)
+    torch.cuda.synchronize(dev)
+    res["first_ok"] = bool(torch.equal(first, want))
+    dist.barrier()
+    skipper = rank == world - 1
+    if not skipper:
+        os.environ["CEA_PEER_WAIT_MS"] = str(wait_ms)
+        t0 = time.perf_counter()
+        out = cea.distributed_kv_attention(*args)
+        torch.cuda.synchronize(dev)
+        res["seconds"] = time.perf_counter() - t0
+        os.environ.pop("CEA_PEER_WAIT_MS")
+        res["all_nan"] = bool(torch.isnan(out.float()).all())
+        res["fault"] = int(ctx.sp._cea_peer_decode.fault[0])
+        res["status"] = _lib.device_status(clear=True, device=dev)
+        # the context still works: a plain attention call on this GPU gives the right answer
+        o_after = cea.attention(q, kl, vl, qp, pl)
+        torch.cuda.synchronize(dev)
+        res["usable"] = bool(torch.isfinite(o_after.float()).all())
+    dist.barrier()  # the skipping rank waited here: the others' kernels are done
+    if not skipper:
+        try:
+            cea.distributed_kv_attention(*args)
+            res["raised"] = False
+        except PeerExchangeTimeout:
+            res["raised"] = True
+        res["disabled"] = bool(getattr(ctx.sp, "_cea_peer_failed", False))
+    dist.barrier()
+    res["skipper"] = skipper
+    return res

@@ -2,6 +2,7 @@
 ring / Ulysses / distributed-KV orchestration against the reference's golden vectors."""
 
 import json
+import os
 
 import numpy as np
 import pytest
@@ -41,6 +42,29 @@ def test_sequence_parallel_orchestration_matches_reference(golden_sp, ci):
             diff = np.where(both, 0, np.abs(got - want))
         assert diff[valid[:, None, :].repeat(want.shape[1], 1)].max() < 1e-12
         assert res["stats"]["sp.send"]["calls"] >= world - 1
+
+
+REFERENCE_ROOT = os.environ.get("COLLAB_INFER_REFERENCE", "/root/reference")
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REFERENCE_ROOT, "collab_infer")),
+                    reason="the reference tree (collab_infer) is not present")
+@pytest.mark.parametrize("ci", [1, 2])
+def test_sequence_parallel_with_reference_communicator(golden_sp, ci):
+    """Drop-in under CollabEngine: ring, Ulysses and distributed-KV decode given collab_infer's own
+    Communicator (built by its ParallelContext) match the reference's golden outputs, and the traffic is
+    booked in the reference's CommStats."""
+    world, kind, weights, causal = CASES[ci]
+    gold = golden_sp[f"sp{ci}"]
+    pos = torch.from_numpy(golden_sp["sp"]["pos"])
+    lay = SequenceLayout(pos.shape[1], world, weights, kind)
+    for r, res in enumerate(_run(W.sp_worker, world, kind, weights, causal, REFERENCE_ROOT)):
+        valid = lay.shard(pos, r).numpy() >= 0
+        for key in ("ring", "ulysses"):
+            assert np.abs(res[key] - gold[f"r{r}/{key}"])[valid].max() < 1e-12, (key, r)
+        assert np.abs(res["dkv"] - gold[f"r{r}/dkv"]).max() < 1e-12
+        assert res["stats"]["sp.send"]["calls"] >= world - 1
+        assert res["stats"]["sp.all_to_all"]["calls"] == 2
 
 
 def test_ulysses_prefill_on_top_of_cache(golden_sp):

@@ -168,3 +168,40 @@ def test_append_split_over_launch_limit(B, n):
     assert torch.equal(kc, k) and torch.equal(vc, v) and torch.equal(pc, pos)
     del kc, vc, pc, cache
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("T,n_new,reserve", [(65, 2, 8), (129, 3, 8), (3000, 1, 4), (1000, 2, 0)])
+def test_decode_writes_its_new_tokens_into_the_cache(T, n_new, reserve):
+    """The decode step's append fused into the split-KV decode kernel (the owner's new tokens are written into
+    the cache by the kernel that reads it): output and cache contents bit-identical to a separate append
+    followed by the decode, with the new keys straddling a split boundary (T = 65: keys 63 and 64 land in
+    two one-tile splits), several new tokens, and a cache without room (reserve 0: the append kernel grows it
+    first)."""
+    import collaborative_edge_system_b200 as cea
+    from collaborative_edge_system_b200.sequence_parallel import distributed_kv_attention
+
+    B, Hq, Hkv, D = 3, 8, 2, 128
+    g = torch.Generator().manual_seed(T + n_new)
+    k = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16).to(DEV)
+    v = torch.randn(B, T, Hkv, D, generator=g).to(torch.bfloat16).to(DEV)
+    pos = torch.arange(T).repeat(B, 1).to(DEV)
+    pos[2, :5] = -1  # a left-padded sequence
+    q = torch.randn(B, n_new, Hq, D, generator=g).to(torch.bfloat16).to(DEV)
+    comm = cea.ParallelContext(1, 1, 1, device=DEV).sp
+    old, new = slice(0, T - n_new), slice(T - n_new, T)
+    fused, plain = LayerKVCache(reserve), LayerKVCache(reserve)
+    for c in (fused, plain):
+        c.append(k[:, old], v[:, old], pos[:, old])
+    assert (fused.capacity - len(fused) >= n_new) == (reserve >= n_new)  # room: the kernel writes the tokens
+    out_f = ring_decode_attention(q, k[:, new], v[:, new], pos[:, new], fused, comm, 0)
+    plain.append(k[:, new], v[:, new], pos[:, new])
+    kc, vc, pc = plain.view()
+    out_p = distributed_kv_attention(q, kc, vc, pos[:, new], pc, comm)
+    torch.cuda.synchronize()
+    assert torch.equal(out_f, out_p)
+    for a, b in zip(fused.view(), plain.view()):
+        assert torch.equal(_bits(a), _bits(b))
+    assert len(fused) == len(plain) == T and fused.capacity == plain.capacity
+    ref = oracle.attention(q.double().cpu().numpy(), k.double().cpu().numpy(), v.double().cpu().numpy(),
+                           pos[:, new].cpu().numpy(), pos.cpu().numpy(), True)
+    assert np.abs(out_f.double().cpu().numpy() - ref).max() < 2e-2

@@ -63,3 +63,31 @@ def test_peer_memory_decode_merge_matches_all_gather_path(world):
         assert used, "peer-memory exchange was not set up"
         assert res == [True, True, True], res
         assert status == 0
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_drop_in_with_reference_communicator_surface(world):
+    """The SP functions given a communicator with only collab_infer's Communicator surface (what CollabEngine
+    builds) run over NCCL and match the oracle; traffic is booked in the caller's CommStats."""
+    for res in _run(W.ref_surface_worker, world):
+        assert res["ring_out"] < 2e-2 and res["ring_lse"] < 1e-3, res
+        assert res["ulysses"] < 2e-2 and res["decode"] < 2e-2, res
+        assert res["stats"]["sp.send"]["calls"] == world - 1
+        assert res["stats"]["sp.all_to_all"]["calls"] == 2
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_exchange_timeout_is_reported_not_hung(world):
+    """A rank that skips a decode call (made on the host): the others' bounded waits run out after a short
+    limit set at run time, they return with NaN rows, CEA_DEV_TIMEOUT_PEER in the fault word and the device
+    status, a usable context, and their next call raises once."""
+    from collaborative_edge_system_b200 import _lib
+
+    for res in _run(W.peer_timeout_worker, world, 300):
+        assert res["first_ok"]
+        if res["skipper"]:
+            continue
+        assert res["all_nan"] and res["usable"], res
+        assert res["fault"] == _lib.DEV_TIMEOUT_PEER and res["status"] == _lib.DEV_TIMEOUT_PEER, res
+        assert 0.25 < res["seconds"] < 10.0, res
+        assert res["raised"] and res["disabled"], res

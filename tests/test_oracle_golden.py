@@ -157,3 +157,18 @@ def test_oracle_ring_with_compressed_wire(golden_wire, name):
         assert np.abs(o - want).max() <= tol, (r, np.abs(o - want).max())
     # the rounding is visible: without it some rank's result moves far past the tolerance
     assert any(np.abs(p[0] - w[0]).max() > 1e-4 * max(1.0, float(np.abs(w[0]).max())) for p, w in zip(plain, res))
+
+
+def test_oracle_config1_full_shape(golden_config1):
+    """Config 1 (fp32, B1, 8/8 heads, head_dim 64, 2048 tokens, causal) at its full shape: the oracle against the
+    reference's own output rows and LSE (``tests/golden/make_golden_config1.py``)."""
+    from make_golden_config1 import checksums, config1_inputs
+
+    gold = golden_config1
+    q, k, v, pos = config1_inputs()
+    assert np.allclose(checksums(q, k, v), gold["checksums"], rtol=1e-12, atol=0)
+    rows = gold["rows"]
+    o, l = oracle.attention_with_lse(q[:, rows].numpy(), k.numpy(), v.numpy(), pos[:, rows].numpy(), pos.numpy(),
+                                     True)
+    assert np.abs(o - gold["out_rows"]).max() < 1e-5
+    assert np.abs(l - gold["lse"][:, :, rows]).max() < 1e-5
