@@ -236,7 +236,26 @@ def bench_prefill(cea, rank, world, dev, steps, warmup):
     # our kernels per attention call: query and key tile statistics, the per-query-tile key range,
     # then the tcgen05 kernel
     gpu_launches = steps * n_attn * 4
+    # per ring step (N > 1): the attention launch, and the gap before the next one on the compute stream (waiting
+    # for the K/V block in flight and unpacking it); averaged over the timed steps, max over ranks
+    ring = None
+    if n_attn > 1:
+        attn, wait = [0.0] * n_attn, [0.0] * n_attn
+        for st in range(steps):
+            calls = ev[launches_before + st * n_attn : launches_before + (st + 1) * n_attn]
+            for t, (s, e) in enumerate(calls):
+                attn[t] += s.elapsed_time(e) / steps
+                if t:
+                    wait[t] += calls[t - 1][1].elapsed_time(s) / steps
+        vals = torch.tensor(attn + wait, device=dev)
+        if world > 1:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        ring = {"attn_ms": [round(x, 4) for x in vals[:n_attn].tolist()],
+                "wait_ms": [round(x, 4) for x in vals[n_attn + 1 :].tolist()],
+                "note": "per ring step, mean over timed steps, max over ranks; wait = gap between consecutive "
+                        "attention launches on the compute stream"}
     return {
+        "ring_steps": ring,
         "ms_per_step": ms / steps,
         "tflops": total_flops * steps / (ms / 1e3) / 1e12,
         "kernel_ms_per_step": kern_ms_per_step,
@@ -348,6 +367,39 @@ def bench_ulysses(cea, rank, world, dev, steps, warmup):
             "ms_per_step": ms / steps, "steps": steps,
             "config": {"batch": UL_B, "seq_len": UL_S, "q_heads": UL_H, "kv_heads": UL_H, "head_dim": D,
                        "seq_sizes": seq, "heads_per_rank": [hs.q_count for hs in heads]}}
+
+
+# ----------------------------------------------------------------------------- ours: config 1 (fp32)
+def bench_config1(cea, rank, world, dev, steps, warmup):
+    """Config 1 at its shape: fp32 ring attention, B1, 8/8 heads, D=64, 2048 tokens split over the ranks
+    (contiguous), causal, with its LSE (the fp32 CUDA-core kernel; 4.30 GFLOP per call)."""
+    S, H, Dh = 2048, 8, 64
+    layout = cea.SequenceLayout(S, world)
+    g = torch.Generator(device=dev).manual_seed(11)
+    q, k, v = (torch.randn(1, S, H, Dh, generator=g, device=dev) for _ in range(3))
+    pos = torch.arange(S, device=dev).view(1, S)
+    ql, kl, vl, pl = (layout.shard(t, rank).contiguous() for t in (q, k, v, pos))
+    comm = cea.ParallelContext(1, world, 1, device=dev).sp
+    reps = 10 * max(1, steps)
+
+    def step():
+        return cea.ring_attention(ql, kl, vl, pl, pl, comm, layout.sizes, causal=True, return_lse=True)
+
+    for _ in range(warmup):
+        step()
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(reps):
+        step()
+    t1.record()
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world, dev) / reps
+    flops = 4.0 * H * Dh * S * (S + 1) / 2
+    return {"metric": "config 1 fp32 ring attention TFLOP/s", "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ms, "steps": reps, "dtype": "f32",
+            "config": {"batch": 1, "seq_len": S, "q_heads": H, "kv_heads": H, "head_dim": Dh, "layout": "contiguous",
+                       "parallelism": f"sp{world}", "kernel": "attn_simt_kernel"}}
 
 
 # ----------------------------------------------------------------------------- ours: decode
@@ -788,6 +840,7 @@ def main():
     pre = bench_prefill(cea, rank, world, dev, args.steps, warmup)
     e2e = bench_prefill_e2e(cea, rank, world, dev, args.steps, warmup, pre["layout"], pre["tensors"], pre["comm"])
     del pre["tensors"]
+    c1 = bench_config1(cea, rank, world, dev, args.steps, warmup)
     dec = None if args.no_decode else bench_decode(cea, rank, world, dev)
     uly = None if args.no_ulysses else bench_ulysses(cea, rank, world, dev, args.steps, warmup)
     llama = None
@@ -828,6 +881,10 @@ def main():
         "clocks": {k: pre["clocks"][k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
         "device_status": status,
     }
+    if pre["ring_steps"] is not None:
+        line["ring_steps"] = pre["ring_steps"]
+    if c1 is not None:
+        line["config1"] = c1
     if dec is not None:
         line["decode"] = {"metric": "split-KV decode tok/s", "value": dec["tok_per_s"], "unit": "tok/s",
                           "ms_per_step": dec["ms_per_step"], "steps": DEC_STEPS,
