@@ -44,6 +44,12 @@ constexpr int kKProducerWarp = 8;  // Q tiles and the K ring
 constexpr int kMmaWarp = 9;         // MMA issuer of half 0; allocates TMEM
 constexpr int kVProducerWarp = 10;  // the V ring
 constexpr int kMmaWarp1 = 11;       // MMA issuer of half 1
+// setmaxnreg split: softmax warpgroups 216, producers and issuers 72, drawn from the 168 registers per thread
+// the launch gives (the most __launch_bounds__(384, 1) allows); the host checks the built count
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsSoftmax = 216;
+constexpr int kRegsOther = 72;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kLaunchRegs * NUM_THREADS, "register split");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPCol = 64;  // P_h columns within S_h (128 keys x 16 bit = 64 columns)
 constexpr float kRescaleThreshold = 8.0f;
@@ -215,7 +221,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp >= kKProducerWarp) {
     // ================================================================ warpgroup 2
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
     if ((warp == kKProducerWarp || warp == kVProducerWarp) && lane == 0) {
       // ---------------------------------------------------------- TMA producers: Q + K ring, V ring
       const bool is_k = warp == kKProducerWarp;
@@ -327,7 +333,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ================================================================ warpgroups 0, 1: softmax + epilogue
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     const int h = warp >> 2;
     const bool active = h == 0 || active1;
     const int row = threadIdx.x & 127;

@@ -242,6 +242,17 @@ int launch_empty(const cea_attn_params* p, cudaStream_t s) {
   return cuda_check("fill_empty_kernel");
 }
 
+// The kernel's setmaxnreg split draws on the registers it is launched with; a build that gave it fewer would
+// leave the softmax warps waiting for registers forever, so refuse to launch it.
+int check_launch_regs(const void* kernel, int expected) {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, kernel) != cudaSuccess) return cuda_check("cudaFuncGetAttributes");
+  if (a.numRegs != expected)
+    return fail(CEA_ERR_UNSUPPORTED, "prefill kernel built with %d registers per thread, its register split needs %d",
+                a.numRegs, expected);
+  return CEA_OK;
+}
+
 int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   const size_t need = tc_stats_bytes(p);
   if (p->workspace == nullptr || p->workspace_bytes < need)
@@ -309,6 +320,7 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
 #define CEA_TC2(DD, BF)                                                                                        \
   do {                                                                                                         \
     auto k = tc2::attn_fwd_tc2_kernel<DD, BF>;                                                                 \
+    if (int e = check_launch_regs(reinterpret_cast<const void*>(k), tc2::kLaunchRegs)) return e;              \
     allow_smem(k, tc2::Layout<DD>::SMEM_ALLOC);                                                                \
     k<<<static_cast<unsigned>(grid2), tc2::NUM_THREADS, tc2::Layout<DD>::SMEM_ALLOC, s>>>(mq, mk, mv, pp);     \
   } while (0)
