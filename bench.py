@@ -745,6 +745,9 @@ def ncu_case(which: str, warmup: int) -> None:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(7)
+    if which not in ("prefill", "decode"):
+        ncu_small_kernels(which, dev, warmup)
+        return
     if which == "prefill":
         S = 16384
         q = (torch.randn(1, S, HQ, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
@@ -765,6 +768,76 @@ def ncu_case(which: str, warmup: int) -> None:
     torch.cuda.synchronize()
 
 
+def ncu_small_kernels(which: str, dev, warmup: int) -> None:
+    """Small cases of the path's other kernels for ncu captures (inputs beyond L2, a few GB at most).
+
+    merge: merge_attention of two [1, 16384, 32, 128] fp32 partials (merge_kernel); ulysses: the Ulysses pack of
+    batch 2, 8192 tokens, 32 MHA heads into 4 peers' blocks and the unpack of the result (copy_segments_kernel);
+    wire: the ring's K||V pack of a [1, 65536, 8, 128] fp32 block into a bf16 wire (wire_cast_kernel);
+    peer: the decode exchange's merge on one rank (peer_merge_kernel, n = 1, config 4's 16 x 32 rows);
+    simt: config 1, fp32, 2048 tokens, 8/8 heads, D = 64 (attn_simt_kernel); llama: one decoder layer's
+    add_rmsnorm, rope and silu_mul at 32768 tokens of LLaMA-3-8B (llama_ops kernels).
+    """
+    import collaborative_edge_system_b200 as cea
+    from collaborative_edge_system_b200 import _lib
+
+    g = torch.Generator(device=dev).manual_seed(3)
+    reps = warmup + 1
+    if which == "merge":
+        o = [torch.randn(1, 16384, HQ, D, generator=g, device=dev) for _ in range(2)]
+        l = [torch.randn(1, HQ, 16384, generator=g, device=dev) for _ in range(2)]
+        for _ in range(reps):
+            cea.merge_attention(o[0], l[0], o[1], l[1])
+    elif which == "ulysses":
+        from collaborative_edge_system_b200.sequence_parallel import _copy_segments
+
+        q = torch.randn(2, 8192, 32, D, generator=g, device=dev).to(torch.bfloat16)
+        shards = cea.partition_heads(32, 32, 4)
+        send = torch.empty(2 * 8192 * 32 * D, dtype=torch.bfloat16, device=dev)
+        pairs, off = [], 0
+        for sh in shards:
+            blk = send[off : off + 2 * 8192 * sh.q_count * D].view(2, 8192, sh.q_count, D)
+            pairs.append((q[:, :, sh.q_start : sh.q_start + sh.q_count], blk))
+            off += blk.numel()
+        for _ in range(reps):
+            _copy_segments(pairs)
+    elif which == "wire":
+        from collaborative_edge_system_b200.sequence_parallel import _pack_wire
+
+        k, v = (torch.randn(1, 65536, HKV, D, generator=g, device=dev) for _ in range(2))
+        for _ in range(reps):
+            _pack_wire(k, v, torch.bfloat16)
+    elif which == "peer":
+        W, rows = D + 4, DEC_B * HQ
+        mem = torch.randn(2 * rows * W + 2, generator=g, device=dev)
+        mem[2 * rows * W :] = 0
+        out = torch.empty(DEC_B, 1, HQ, D, dtype=torch.bfloat16, device=dev)
+        base = mem.data_ptr()
+        for e in range(1, reps + 1):
+            _lib.peer_merge(1, 0, [base], [base + 2 * rows * W * 4], e, W, out)
+    elif which == "simt":
+        q, k, v = (torch.randn(1, 2048, 8, 64, generator=g, device=dev) for _ in range(3))
+        pos = torch.arange(2048, device=dev).view(1, 2048)
+        for _ in range(reps):
+            cea.attention_with_lse(q, k, v, pos, pos, causal=True)
+    elif which == "llama":
+        S, Hd, F = 32768, 4096, 14336
+        x = torch.randn(S, Hd, generator=g, device=dev).to(torch.bfloat16)
+        dx = torch.randn(S, Hd, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.ones(Hd, device=dev, dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        qkv = torch.randn(1, S, 48, D, generator=g, device=dev).to(torch.bfloat16)
+        pos = torch.arange(S, device=dev).view(1, S)
+        inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+        gu = torch.randn(S, 2 * F, generator=g, device=dev).to(torch.bfloat16)
+        act = torch.empty(S, F, device=dev, dtype=torch.bfloat16)
+        for _ in range(reps):
+            _lib.add_rmsnorm(x, dx, w, y, 1e-5)
+            _lib.rope(qkv[:, :, :32], qkv[:, :, 32:40], pos, inv)
+            _lib.silu_mul(gu[:, :F], gu[:, F:], act)
+    torch.cuda.synchronize()
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -781,7 +854,8 @@ def main():
     ap.add_argument("--llama-tp", type=int, default=1, help="tensor-parallel size of the --llama run")
     ap.add_argument("--cpu-configs", action="store_true",
                     help="time the reference's own CPU/gloo path per configuration (host cores only)")
-    ap.add_argument("--ncu-case", choices=["prefill", "decode"], default=None,
+    ap.add_argument("--ncu-case", choices=["prefill", "decode", "merge", "ulysses", "wire", "peer", "simt", "llama"],
+                    default=None,
                     help="run a small case of one kernel for an ncu capture (no timing, no JSON line)")
     args = ap.parse_args()
     if args.ncu_case:

@@ -826,13 +826,27 @@ int cea_add_rmsnorm(const cea_rmsnorm_params* p, void* stream) {
                          p->resid_stride, p->delta_stride, p->y_stride, p->eps};
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(p->rows, 148 * 16));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // vectorised form: 16-byte rows that fit in the threads' registers
+  const int eb = elem_bytes(p->dtype), n = 16 / eb;
+  const bool vec = p->h % n == 0 && p->h <= int64_t(cea::llama::kNormThreads) * cea::llama::kNormMaxVecs * n &&
+                   aligned16(p->resid) && aligned16(p->weight) && aligned16(p->y) &&
+                   (p->delta == nullptr || aligned16(p->delta)) && p->resid_stride % n == 0 && p->y_stride % n == 0 &&
+                   (p->delta == nullptr || p->delta_stride % n == 0);
+#define CEA_NORM(T)                                                                              \
+  do {                                                                                           \
+    if (vec)                                                                                     \
+      cea::llama::add_rmsnorm_vec_kernel<T><<<grid, cea::llama::kNormThreads, 0, s>>>(a);        \
+    else                                                                                         \
+      cea::llama::add_rmsnorm_kernel<T><<<grid, cea::llama::kNormThreads, 0, s>>>(a);            \
+  } while (0)
   switch (p->dtype) {
-    case CEA_F32: cea::llama::add_rmsnorm_kernel<float><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
-    case CEA_F16: cea::llama::add_rmsnorm_kernel<__half><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
-    case CEA_BF16: cea::llama::add_rmsnorm_kernel<__nv_bfloat16><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
-    case CEA_F64: cea::llama::add_rmsnorm_kernel<double><<<grid, cea::llama::kNormThreads, 0, s>>>(a); break;
+    case CEA_F32: CEA_NORM(float); break;
+    case CEA_F16: CEA_NORM(__half); break;
+    case CEA_BF16: CEA_NORM(__nv_bfloat16); break;
+    case CEA_F64: CEA_NORM(double); break;
     default: return fail(CEA_ERR_UNSUPPORTED, "%s: dtype %d", what, p->dtype);
   }
+#undef CEA_NORM
   return cuda_check(what);
 }
 
@@ -860,14 +874,16 @@ int cea_rope(const cea_rope_params* p, void* stream) {
   a.B = p->B;
   a.S = p->S;
   a.D = p->D;
-  const dim3 grid(static_cast<unsigned>(std::min<int64_t>((most + cea::llama::kEltThreads - 1) / cea::llama::kEltThreads,
-                                                          148 * 8)), 2);
+  // one thread per (token, pair): the token's cos / sin serve every q and k head
+  const int64_t pairs = static_cast<int64_t>(p->B) * p->S * (p->D / 2);
+  const unsigned grid = static_cast<unsigned>(
+      std::min<int64_t>((pairs + cea::llama::kEltThreads - 1) / cea::llama::kEltThreads, 148 * 32));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (p->dtype) {
-    case CEA_F32: cea::llama::rope_kernel<float><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
-    case CEA_F16: cea::llama::rope_kernel<__half><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
-    case CEA_BF16: cea::llama::rope_kernel<__nv_bfloat16><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
-    case CEA_F64: cea::llama::rope_kernel<double><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F32: cea::llama::rope_token_kernel<float><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F16: cea::llama::rope_token_kernel<__half><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_BF16: cea::llama::rope_token_kernel<__nv_bfloat16><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F64: cea::llama::rope_token_kernel<double><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
     default: return fail(CEA_ERR_UNSUPPORTED, "%s: dtype %d", what, p->dtype);
   }
   return cuda_check(what);
@@ -880,16 +896,28 @@ int cea_silu_mul(const cea_silu_mul_params* p, void* stream) {
   if (p->rows * p->n == 0) return CEA_OK;
   if (!p->gate || !p->up || !p->out) return fail(CEA_ERR_INVALID, "%s: null pointer", what);
   cea::llama::SiluArgs a{p->gate, p->up, p->out, p->rows, p->n, p->in_stride, p->out_stride};
-  const unsigned grid = static_cast<unsigned>(
-      std::min<int64_t>((p->rows * p->n + cea::llama::kEltThreads - 1) / cea::llama::kEltThreads, 148 * 8));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int eb = elem_bytes(p->dtype), vn = 16 / eb;
+  const bool vec = p->n % vn == 0 && p->in_stride % vn == 0 && p->out_stride % vn == 0 && aligned16(p->gate) &&
+                   aligned16(p->up) && aligned16(p->out);
+  const unsigned grid = vec ? static_cast<unsigned>(std::min<int64_t>(p->rows, 148 * 16))
+                            : static_cast<unsigned>(std::min<int64_t>(
+                                  (p->rows * p->n + cea::llama::kEltThreads - 1) / cea::llama::kEltThreads, 148 * 8));
+#define CEA_SILU(T)                                                                               \
+  do {                                                                                            \
+    if (vec)                                                                                      \
+      cea::llama::silu_mul_vec_kernel<T><<<grid, cea::llama::kEltThreads, 0, s>>>(a);             \
+    else                                                                                          \
+      cea::llama::silu_mul_kernel<T><<<grid, cea::llama::kEltThreads, 0, s>>>(a);                 \
+  } while (0)
   switch (p->dtype) {
-    case CEA_F32: cea::llama::silu_mul_kernel<float><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
-    case CEA_F16: cea::llama::silu_mul_kernel<__half><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
-    case CEA_BF16: cea::llama::silu_mul_kernel<__nv_bfloat16><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
-    case CEA_F64: cea::llama::silu_mul_kernel<double><<<grid, cea::llama::kEltThreads, 0, s>>>(a); break;
+    case CEA_F32: CEA_SILU(float); break;
+    case CEA_F16: CEA_SILU(__half); break;
+    case CEA_BF16: CEA_SILU(__nv_bfloat16); break;
+    case CEA_F64: CEA_SILU(double); break;
     default: return fail(CEA_ERR_UNSUPPORTED, "%s: dtype %d", what, p->dtype);
   }
+#undef CEA_SILU
   return cuda_check(what);
 }
 

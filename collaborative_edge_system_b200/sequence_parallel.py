@@ -264,7 +264,8 @@ def ulysses_attention(
         p_att = torch.cat([past[2].to(pos_f.device), pos_f], dim=1)
     o = attention(q_f, k_att, v_att, pos_f, p_att, causal=causal, scale=scale, kv_map=me.kv_map, kv_block=kv_block)
     out = ulysses_gather(o, comm, seq_sizes, head_shards)
-    return out, (k_f.contiguous(), v_f.contiguous(), pos_f)
+    # this rank's KV heads over the new tokens as views of the received buffer (a KV cache copies them anyway)
+    return out, (k_f, v_f, pos_f)
 
 
 def gather_heads(out_local: torch.Tensor, comm: Communicator, head_shards: Sequence[HeadShard]) -> torch.Tensor:
