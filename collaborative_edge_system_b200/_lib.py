@@ -20,7 +20,7 @@ F32, F16, BF16, F64 = 0, 1, 2, 3
 _DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
 
 CEA_OK, CEA_ERR_INVALID, CEA_ERR_UNSUPPORTED, CEA_ERR_CUDA, CEA_ERR_WORKSPACE, CEA_ERR_DEVICE, CEA_ERR_NCCL = range(7)
-ABI_VERSION = 6
+ABI_VERSION = 7
 NCCL_ID_BYTES = 128
 MAX_PEERS = 16
 IPC_HANDLE_BYTES = 64
@@ -72,6 +72,8 @@ class AttnParams(ctypes.Structure):
         ("new_v_stride", _i64x3),
         ("new_pos_stride", _i64x2),
         ("n_new", ctypes.c_int32),
+        ("acc_in", ctypes.c_void_p),
+        ("acc_stride", _i64x3),
     ]
 
 
@@ -354,10 +356,12 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 def attn_params(
     q, k, v, q_pos, k_pos, out, lse, *, causal: bool, scale: float, kv_map: Optional[torch.Tensor], accumulate: bool,
-    append=None,
+    append=None, acc_in: Optional[torch.Tensor] = None,
 ) -> AttnParams:
     """Parameters of one attention call.  ``append = (k_new, v_new, pos_new)``: the last ``k_new.shape[1]``
-    keys are this decode step's new tokens, written into ``k``/``v``/``k_pos`` by the decode kernel."""
+    keys are this decode step's new tokens, written into ``k``/``v``/``k_pos`` by the decode kernel.
+    ``acc_in`` (fp32, the shape of ``out``): with ``accumulate`` and a 16-bit ``out``, the running result is
+    read from it and the merged result written to ``out`` in the input dtype."""
     B, Sq, Hq, D = q.shape
     Sk, Hkv = k.shape[1], k.shape[2]
     for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
@@ -389,6 +393,11 @@ def attn_params(
         p.new_v_stride = _i64x3(nv.stride(0), nv.stride(1), nv.stride(2))
         p.new_pos_stride = _i64x2(npos.stride(0), npos.stride(1))
         p.n_new = nk.shape[1]
+    if acc_in is not None:
+        if acc_in.dtype != torch.float32 or tuple(acc_in.shape) != tuple(out.shape) or acc_in.stride(-1) != 1:
+            raise ValueError("acc_in must be fp32, shaped like out and contiguous along the head dimension")
+        p.acc_in = acc_in.data_ptr()
+        p.acc_stride = _i64x3(acc_in.stride(0), acc_in.stride(1), acc_in.stride(2))
     return p
 
 

@@ -144,6 +144,7 @@ def attend_into(
     kv_map: KVMap = None,
     accumulate: bool = False,
     append: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+    acc_in: Optional[torch.Tensor] = None,
 ) -> None:
     """Write attention (and lse) into preallocated tensors; ``accumulate`` merges exactly.
 
@@ -157,8 +158,15 @@ def attend_into(
     tokens: the split-KV decode kernel writes them into the cache as it reads
     it, which replaces the separate append launch (``models/cache.py:51-62``).
     Where another kernel serves the call, the tokens are appended first.
+
+    ``acc_in`` (fp32, shaped like ``out``), with ``accumulate=True`` and a
+    16-bit ``out``: the running result is read from ``acc_in`` and the merged
+    result written to ``out`` in ``q``'s dtype, which fuses the last ring
+    step's merge with the final ``out.to(q.dtype)``
+    (``parallel/sequence_parallel.py:117-130``).  Where the tcgen05 kernel does
+    not serve the call, the merge goes into ``acc_in``, then into ``out``.
     """
-    dev = _lib.require_cuda(q, k, v, out, lse)
+    dev = _lib.require_cuda(q, k, v, out, lse, acc_in)
     _check_shapes(q, k, v, q_pos, k_pos)
     if append is not None and (k.dtype != q.dtype or k_pos.dtype != torch.int64 or k_pos.device != dev):
         _append_tokens(k, v, k_pos, append)  # the kernel would see converted copies, not the cache
@@ -174,6 +182,17 @@ def attend_into(
         _append_tokens(k, v, k_pos, append)
         p = _lib.attn_params(q, k, v, q_pos, k_pos, out, lse, causal=causal, scale=scale, kv_map=kvm,
                              accumulate=accumulate)
+    if acc_in is not None:
+        if not accumulate:
+            raise ValueError("acc_in is the running result of an accumulating call")
+        p = _lib.attn_params(q, k, v, q_pos, k_pos, out, lse, causal=causal, scale=scale, kv_map=kvm,
+                             accumulate=True, acc_in=acc_in)
+        if k.shape[1] == 0 or _lib.kernel_kind(p) != _lib.KIND_TC:
+            p = _lib.attn_params(q, k, v, q_pos, k_pos, acc_in, lse, causal=causal, scale=scale, kv_map=kvm,
+                                 accumulate=True)
+            _lib.attn_fwd(p, dev)
+            out.copy_(acc_in)
+            return
     _lib.attn_fwd(p, dev)
 
 

@@ -102,6 +102,9 @@ struct AttnArgs {
   int B, Sq, Sk, Hq, Hkv, group, nqt, nkt;
   float scale_log2;
   int causal, out_dtype, accumulate;
+  // accumulate with a 16-bit out: the stored fp32 result is read from here instead of out (null: from out)
+  const float* acc_in;
+  int64_t a_sb, a_ss, a_sh;
 };
 
 // warp-uniform bounded wait: every lane waits, the warp continues only if all succeeded
@@ -463,7 +466,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ok = warp_wait(bar(L::B_PVDONE + h), (it - 1) & 1, abort_flag, CEA_DEV_TIMEOUT_SOFTMAX);
       tc_fence_after();
     }
-    if (ok && active && !(it == 0 && p.accumulate)) {
+    // a row that saw no key keeps its stored result, which with acc_in still has to reach out
+    if (ok && active && !(it == 0 && p.accumulate && p.acc_in == nullptr)) {
       const int hh = h == 0 ? head0 : head1;
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const float lse_row = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
@@ -513,11 +517,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + obase + c * 16;
 #pragma unroll
           for (int e = 0; e < 16; e += 8) {
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(o[e + j]) * c_new;
+            if (p.acc_in != nullptr) {  // merge the running fp32 result and cast in one pass
+              const float* src = p.acc_in + b * p.a_sb + static_cast<int64_t>(q_row) * p.a_ss + hh * p.a_sh + c * 16 + e;
+              const float4 a0 = *reinterpret_cast<const float4*>(src);
+              const float4 a1 = *reinterpret_cast<const float4*>(src + 4);
+              f[0] += a0.x * w_old;
+              f[1] += a0.y * w_old;
+              f[2] += a0.z * w_old;
+              f[3] += a0.w * w_old;
+              f[4] += a1.x * w_old;
+              f[5] += a1.y * w_old;
+              f[6] += a1.z * w_old;
+              f[7] += a1.w * w_old;
+            }
             uint4 v;
-            v.x = pack2(__uint_as_float(o[e]) * c_new, __uint_as_float(o[e + 1]) * c_new, kBF16);
-            v.y = pack2(__uint_as_float(o[e + 2]) * c_new, __uint_as_float(o[e + 3]) * c_new, kBF16);
-            v.z = pack2(__uint_as_float(o[e + 4]) * c_new, __uint_as_float(o[e + 5]) * c_new, kBF16);
-            v.w = pack2(__uint_as_float(o[e + 6]) * c_new, __uint_as_float(o[e + 7]) * c_new, kBF16);
+            v.x = pack2(f[0], f[1], kBF16);
+            v.y = pack2(f[2], f[3], kBF16);
+            v.z = pack2(f[4], f[5], kBF16);
+            v.w = pack2(f[6], f[7], kBF16);
             *reinterpret_cast<uint4*>(dst + e) = v;
           }
         }

@@ -112,8 +112,13 @@ int validate(const cea_attn_params* p) {
   if (in < CEA_F32 || in > CEA_F64) return fail(CEA_ERR_INVALID, "unknown input dtype %d", in);
   const bool out_ok = in == CEA_F64 ? (out == CEA_F64) : (out == CEA_F32 || out == in);
   if (!out_ok) return fail(CEA_ERR_UNSUPPORTED, "output dtype %d not available for input dtype %d", out, in);
-  if (p->accumulate && (p->lse == nullptr || (out != CEA_F32 && out != CEA_F64)))
-    return fail(CEA_ERR_INVALID, "accumulate needs lse and an fp32/fp64 output");
+  const bool wide_out = out == CEA_F32 || out == CEA_F64;
+  if (p->acc_in != nullptr && (!p->accumulate || wide_out))
+    return fail(CEA_ERR_INVALID, "acc_in serves accumulate = 1 with a 16-bit output only");
+  if (p->accumulate && (p->lse == nullptr || (!wide_out && p->acc_in == nullptr)))
+    return fail(CEA_ERR_INVALID, "accumulate needs lse and an fp32/fp64 output (or acc_in)");
+  if (p->acc_in != nullptr && p->Sk == 0)
+    return fail(CEA_ERR_UNSUPPORTED, "acc_in with no keys: nothing to merge, copy acc_in to out instead");
   const bool empty = p->B == 0 || p->Sq == 0 || p->Hq == 0;
   if (!empty && (p->out == nullptr || p->q_pos == nullptr || p->q == nullptr))
     return fail(CEA_ERR_INVALID, "null q, out or q_pos");
@@ -138,6 +143,7 @@ bool append_ok(const cea_attn_params* p) {
 enum Kind { kNone = 0, kTc = 1, kDecode = 2, kSimt = 3 };
 
 bool decode_ok(const cea_attn_params* p) {
+  if (p->acc_in != nullptr) return false;
   if (p->in_dtype != CEA_BF16 && p->in_dtype != CEA_F16) return false;
   if (p->D != 64 && p->D != 128) return false;
   if (p->kv_map != nullptr) return false;
@@ -159,11 +165,17 @@ bool tc_ok(const cea_attn_params* p) {
   if (!aligned16(p->out)) return false;
   for (int i = 0; i < 3; ++i)
     if (p->o_stride[i] % vec) return false;
+  if (p->acc_in != nullptr) {  // fp32 rows read as 16-byte vectors
+    if (!aligned16(p->acc_in)) return false;
+    for (int i = 0; i < 3; ++i)
+      if (p->acc_stride[i] % 4) return false;
+  }
   return true;
 }
 
 int select_kind(const cea_attn_params* p) {
   if (p->B == 0 || p->Sq == 0 || p->Hq == 0 || p->Sk == 0) return kNone;
+  if (p->acc_in != nullptr) return tc_ok(p) ? kTc : kSimt;  // only the tcgen05 epilogue reads acc_in
   if (decode_ok(p)) return kDecode;
   if (tc_ok(p)) return kTc;
   return kSimt;
@@ -307,6 +319,10 @@ int launch_tc(const cea_attn_params* p, cudaStream_t s) {
   tp.causal = p->causal;
   tp.out_dtype = p->out_dtype;
   tp.accumulate = p->accumulate;
+  tp.acc_in = p->acc_in;
+  tp.a_sb = p->acc_stride[0];
+  tp.a_ss = p->acc_stride[1];
+  tp.a_sh = p->acc_stride[2];
   const bool bf = p->in_dtype == CEA_BF16;
   // two query tiles per CTA: a GQA head pair when the uniform grouping pairs heads on one KV head, else two
   // adjacent query tiles of one head (an explicit kv_map lives on the device, so it takes the second form)
@@ -542,6 +558,9 @@ int cea_attn_fwd(const cea_attn_params* p, void* stream) {
   if (p->n_new > 0 && kind != kDecode)
     return fail(CEA_ERR_UNSUPPORTED, "the fused cache append runs on the split-KV decode path only "
                                      "(cea_attn_kernel_kind 2); append the tokens separately");
+  if (p->acc_in != nullptr && kind != kTc)
+    return fail(CEA_ERR_UNSUPPORTED, "acc_in runs on the tcgen05 path only (cea_attn_kernel_kind 1): bf16/f16, "
+                                     "D in {64,128}, TMA-aligned operands, 16-byte aligned out and acc_in rows");
   switch (kind) {
     case kDecode:
       return launch_decode(p, s);

@@ -106,6 +106,7 @@ def ring_attention(
     k_cur, v_cur = k, v
     pos = k_pos.to(device=q.device, dtype=torch.int64).contiguous()
     nxt, prv = (r + 1) % n, (r - 1) % n
+    res = out
     for step in range(n):
         pending = None
         if step < n - 1:
@@ -113,12 +114,17 @@ def ring_attention(
             pending = comm.ring_exchange(
                 [wire, pos], nxt, [((2, B, kv_sizes[src], Hkv, D), wire.dtype), ((B, kv_sizes[src]), torch.int64)],
                 prv)
-        attend_into(q, k_cur, v_cur, q_pos, pos, out, lse, causal=causal, scale=scale, kv_map=kv_map,
-                    accumulate=step > 0)
+        if step == n - 1 and q.dtype != acc:
+            # the last step merges into the running fp32 result and writes q.dtype itself: no cast pass
+            res = torch.empty(B, Sq, Hq, D, dtype=q.dtype, device=q.device)
+            attend_into(q, k_cur, v_cur, q_pos, pos, res, lse, causal=causal, scale=scale, kv_map=kv_map,
+                        accumulate=True, acc_in=out)
+        else:
+            attend_into(q, k_cur, v_cur, q_pos, pos, out, lse, causal=causal, scale=scale, kv_map=kv_map,
+                        accumulate=step > 0)
         if pending is not None:
             wire, pos = pending.wait()
             k_cur, v_cur = _unpack_wire(wire, k.dtype)
-    res = out.to(q.dtype)
     return (res, lse) if return_lse else res
 
 

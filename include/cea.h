@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define CEA_ABI_VERSION 6
+#define CEA_ABI_VERSION 7
 
 enum cea_status {
   CEA_OK = 0,
@@ -104,6 +104,14 @@ typedef struct cea_attn_params {
   int64_t new_v_stride[3];
   int64_t new_pos_stride[2];
   int32_t n_new;
+  /* Optional source of the running result for accumulate = 1 with a 16-bit out, served by the tcgen05
+   * prefill path only (cea_attn_kernel_kind 1; other paths fail with CEA_ERR_UNSUPPORTED).  The stored
+   * result is read from acc_in ([B, Sq, Hq, D] F32, element strides b, s, h; rows 16-byte aligned)
+   * instead of out, merged with this call's partial, and written to out in the input dtype; lse is
+   * updated in place.  This fuses the last ring step's merge with the final cast to the activation
+   * dtype (collab_infer parallel/sequence_parallel.py:117-130).  NULL (zero-initialised) disables it. */
+  const float* acc_in;
+  int64_t acc_stride[3];
 } cea_attn_params;
 
 /* Bytes of workspace cea_attn_fwd needs for these parameters (0 if none). */

@@ -29,13 +29,14 @@ def install_oracle_compute():
         return t.detach().cpu().numpy()
 
     def attend_into(q, k, v, q_pos, k_pos, out, lse, *, causal=True, scale=None, kv_map=None, accumulate=False,
-                    append=None):
+                    append=None, acc_in=None):
         if append is not None:  # the new tokens into the last rows of the cache views
             n = append[0].shape[1]
             k[:, -n:], v[:, -n:], k_pos[:, -n:] = append
         o, l = oracle.attention_with_lse(npy(q), npy(k), npy(v), npy(q_pos), npy(k_pos), causal, scale, kv_list(kv_map))
-        if accumulate:
-            o, l = oracle.merge_attention(npy(out).astype(np.float64), npy(lse).astype(np.float64), o, l)
+        if accumulate:  # the running result is in acc_in when given, else in out
+            prev = out if acc_in is None else acc_in
+            o, l = oracle.merge_attention(npy(prev).astype(np.float64), npy(lse).astype(np.float64), o, l)
         out.copy_(torch.from_numpy(o))
         if lse is not None:
             lse.copy_(torch.from_numpy(l))

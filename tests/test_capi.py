@@ -29,7 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.cea_abi_version() == _lib.ABI_VERSION == 6
+    assert lib.cea_abi_version() == _lib.ABI_VERSION == 7
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():

@@ -199,6 +199,61 @@ def test_tc_accumulate_equals_full():
     _cmp(_np(lse), ref_l, 1e-3)
 
 
+@pytest.mark.parametrize("D,split", [(128, "random"), (64, "late"), (96, "late"), (128, "none")])
+def test_accumulate_from_acc_in_writes_input_dtype(D, split):
+    # the last ring step: merge into the fp32 running result held in acc_in and write bf16 to out.  "late"
+    # leaves the first query tiles no visible key in the second call (their rows only copy acc_in), D=96 takes
+    # the fallback (merge into acc_in, then copy), "none" passes no keys at all
+    B, S, Hq, Hkv = 1, 512, 4, 2
+    q, k, v, qp, kp = _inputs(B, S, S, Hq, Hkv, D, torch.bfloat16, seed=6)
+    ref_o, ref_l = _oracle(q, k, v, qp, kp, True)
+    qd, kd, vd, qpd, kpd = (t.to(DEV) for t in (q, k, v, qp, kp))
+    if split == "random":
+        perm = torch.randperm(S, generator=torch.Generator().manual_seed(1))
+        a, b = perm[:300].sort().values, perm[300:].sort().values
+    elif split == "late":
+        a, b = torch.arange(300, S), torch.arange(0, 300)
+    else:
+        a, b = torch.arange(0, 0), torch.arange(0, S)
+    a, b = a.to(DEV), b.to(DEV)
+    acc = torch.empty(B, S, Hq, D, dtype=torch.float32, device=DEV)
+    lse = torch.empty(B, Hq, S, dtype=torch.float32, device=DEV)
+    cea.attend_into(qd, kd[:, b], vd[:, b], qpd, kpd[:, b], acc, lse)
+    # the same merge written in fp32, for the bit-level comparison below
+    acc2, lse2 = acc.clone(), lse.clone()
+    cea.attend_into(qd, kd[:, a], vd[:, a], qpd, kpd[:, a], acc2, lse2, accumulate=True)
+    out = torch.full((B, S, Hq, D), float("nan"), dtype=torch.bfloat16, device=DEV)
+    cea.attend_into(qd, kd[:, a], vd[:, a], qpd, kpd[:, a], out, lse, accumulate=True, acc_in=acc)
+    torch.cuda.synchronize()
+    _cmp(_np(out), ref_o, 2e-2)
+    _cmp(_np(lse), ref_l, 1e-3)
+    assert torch.equal(lse, lse2)
+    # one rounding of the same fp32 value: at most one bf16 step apart, almost always identical
+    diff = (out.float() - acc2.to(torch.bfloat16).float()).abs()
+    assert float(diff.max()) <= float(acc2.abs().max()) * 2.0 ** -7
+    assert float((diff > 0).float().mean()) < 1e-3
+
+
+def test_acc_in_is_refused_where_it_cannot_apply():
+    q, k, v, qp, kp = _inputs(1, 128, 128, 2, 2, 64, torch.bfloat16, seed=3)
+    qd, kd, vd, qpd, kpd = (t.to(DEV) for t in (q, k, v, qp, kp))
+    acc = torch.zeros(1, 128, 2, 64, device=DEV)
+    lse = torch.zeros(1, 2, 128, device=DEV)
+    out32 = torch.empty_like(acc)
+    with pytest.raises(ValueError):  # acc_in is the running result of an accumulating call
+        cea.attend_into(qd, kd, vd, qpd, kpd, torch.empty_like(qd), lse, acc_in=acc)
+    p = _lib.attn_params(qd, kd, vd, qpd, kpd, out32, lse, causal=True, scale=0.125, kv_map=None, accumulate=True,
+                         acc_in=acc)
+    with pytest.raises(ValueError, match="16-bit output"):
+        _lib.attn_fwd(p, qd.device)
+    p = _lib.attn_params(qd[:, :1], kd, vd, qpd[:, :1], kpd, torch.empty_like(qd[:, :1]), lse[:, :, :1], causal=True,
+                         scale=0.125, kv_map=None, accumulate=True, acc_in=acc[:, :1])
+    assert _lib.kernel_kind(p) == _lib.KIND_TC  # never the decode path, which has no acc_in
+    with pytest.raises(RuntimeError, match="split-KV decode"):
+        _lib.attn_fwd(p, qd.device, entry="cea_decode_splitkv")
+    assert _lib.device_status(clear=True) == 0
+
+
 def test_fully_masked_rows_and_blocks():
     # keys all in the future of the queries: every row empty -> out 0, lse -inf (no NaN)
     q, k, v, _, kp = _inputs(1, 128, 256, 2, 1, 128, torch.bfloat16, seed=9)
