@@ -545,8 +545,27 @@ def bench_llama(cea, rank, world, dev, steps, warmup, tp_size=1):
         end.record()
         barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world, dev) / steps
+    tp_info = {}
+    if tp_size > 1:
+        # the share of the TP all-reduces: one [1, s, hidden] bf16 partial summed over the TP group after the
+        # attention output and the MLP down projection of every layer, plus the embedding; timed alone here
+        part = torch.randn(1, layout.sizes[comm.rank], h, device=dev).to(torch.bfloat16) * 1e-3  # summed in place
+        n_ar = 2 * cfg.num_layers + 1
+        with torch.no_grad():
+            for _ in range(3):
+                ctx.tp.all_reduce(part)
+            barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n_ar):
+                ctx.tp.all_reduce(part)
+            b.record()
+            barrier(world)
+        ar_ms = max_over_ranks(a.elapsed_time(b), world, dev)
+        tp_info = {"tp_allreduce": {"calls_per_step": n_ar, "bytes_per_call": part.numel() * 2,
+                                    "ms_per_step_alone": ar_ms, "share_of_step": ar_ms / ms}}
     return {"metric": "LLaMA-3-8B 32K-token prefill tokens/s", "value": LLAMA_S / (ms / 1e3), "unit": "tok/s",
-            "ms_per_step": ms, "model_tflops": total_flops / (ms / 1e3) / 1e12,
+            "ms_per_step": ms, "model_tflops": total_flops / (ms / 1e3) / 1e12, **tp_info,
             "flops_per_step": total_flops, "clocks": clk.summary(),
             "config": {"workload": "LLaMA-3-8B prefill (config 5)", "batch": 1, "seq_len": LLAMA_S,
                        "layers": cfg.num_layers, "hidden": h, "heads": cfg.num_heads, "kv_heads": cfg.num_kv_heads,
