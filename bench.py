@@ -372,7 +372,7 @@ def bench_ulysses(cea, rank, world, dev, steps, warmup):
 # ----------------------------------------------------------------------------- ours: config 1 (fp32)
 def bench_config1(cea, rank, world, dev, steps, warmup):
     """Config 1 at its shape: fp32 ring attention, B1, 8/8 heads, D=64, 2048 tokens split over the ranks
-    (contiguous), causal, with its LSE (the fp32 CUDA-core kernel; 4.30 GFLOP per call)."""
+    (contiguous), causal, with its LSE (the register-tiled fp32 CUDA-core kernel; 4.30 GFLOP per call)."""
     S, H, Dh = 2048, 8, 64
     layout = cea.SequenceLayout(S, world)
     g = torch.Generator(device=dev).manual_seed(11)
@@ -399,7 +399,7 @@ def bench_config1(cea, rank, world, dev, steps, warmup):
     return {"metric": "config 1 fp32 ring attention TFLOP/s", "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
             "ms_per_step": ms, "steps": reps, "dtype": "f32",
             "config": {"batch": 1, "seq_len": S, "q_heads": H, "kv_heads": H, "head_dim": Dh, "layout": "contiguous",
-                       "parallelism": f"sp{world}", "kernel": "attn_simt_kernel"}}
+                       "parallelism": f"sp{world}", "kernel": "attn_f32_kernel"}}
 
 
 # ----------------------------------------------------------------------------- ours: decode
@@ -794,7 +794,7 @@ def ncu_small_kernels(which: str, dev, warmup: int) -> None:
     batch 2, 8192 tokens, 32 MHA heads into 4 peers' blocks and the unpack of the result (copy_segments_kernel);
     wire: the ring's K||V pack of a [1, 65536, 8, 128] fp32 block into a bf16 wire (wire_cast_kernel);
     peer: the decode exchange's merge on one rank (peer_merge_kernel, n = 1, config 4's 16 x 32 rows);
-    simt: config 1, fp32, 2048 tokens, 8/8 heads, D = 64 (attn_simt_kernel); llama: one decoder layer's
+    simt: config 1, fp32, 2048 tokens, 8/8 heads, D = 64 (attn_f32_kernel); llama: one decoder layer's
     add_rmsnorm, rope and silu_mul at 32768 tokens of LLaMA-3-8B (llama_ops kernels).
     """
     import collaborative_edge_system_b200 as cea

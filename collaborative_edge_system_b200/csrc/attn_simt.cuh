@@ -1,7 +1,7 @@
-// Attention with log-sum-exp on the CUDA cores, for the cases the tensor-core
-// kernels do not take: fp32 (collab_infer's config-1 precision, checked at
-// 1e-4 / 1e-5), fp64 (the reference's own test precision) and head dims other
-// than 64/128.  Same masking, empty-row and accumulate semantics as the
+// Attention with log-sum-exp on the CUDA cores, for the cases neither the tensor-core
+// kernels nor the register-tiled fp32 kernel (attn_f32.cuh, fp32 at head dims 32/64)
+// take: fp64 (the reference's own test precision), fp32 at other head dims (checked
+// at 1e-4 / 1e-5), and 16-bit inputs at head dims other than 64/128.  Same masking, empty-row and accumulate semantics as the
 // tcgen05 kernel; exp in the accumulation type (expf / exp).
 //
 // CTA = 128 threads = 16 query rows x 8 threads; keys in blocks of 32 staged

@@ -10,6 +10,7 @@
 #include <string>
 #include <type_traits>
 
+#include "attn_f32.cuh"
 #include "attn_simt.cuh"
 #include "attn_tc2.cuh"
 #include "cea_common.cuh"
@@ -470,6 +471,24 @@ int launch_simt_d(const simt::Params& sp, const cea_attn_params* p, cudaStream_t
   return cuda_check("attn_simt_kernel");
 }
 
+// the register-tiled fp32 kernel: fp32 in and out, head dim 32 or 64, K/V rows 16-byte aligned (cp.async)
+bool f32_ok(const cea_attn_params* p) {
+  if (p->in_dtype != CEA_F32 || p->out_dtype != CEA_F32 || (p->D != 32 && p->D != 64)) return false;
+  if (!aligned16(p->k) || !aligned16(p->v)) return false;
+  for (int i = 0; i < 3; ++i)
+    if (p->k_stride[i] % 4 || p->v_stride[i] % 4) return false;
+  return true;
+}
+
+template <int DD>
+int launch_f32(const simt::Params& sp, const cea_attn_params* p, cudaStream_t s) {
+  auto k = f32k::attn_f32_kernel<DD>;
+  allow_smem(k, static_cast<int>(f32k::Smem<DD>::BYTES));
+  const dim3 grid((p->Sq + f32k::ROWS - 1) / f32k::ROWS, p->Hq, p->B);
+  k<<<grid, f32k::NT, f32k::Smem<DD>::BYTES, s>>>(sp);
+  return cuda_check("attn_f32_kernel");
+}
+
 int launch_simt(const cea_attn_params* p, cudaStream_t s) {
   simt::Params sp;
   sp.q = p->q;
@@ -509,6 +528,7 @@ int launch_simt(const cea_attn_params* p, cudaStream_t s) {
   sp.scale = p->scale;
   sp.causal = p->causal;
   sp.accumulate = p->accumulate;
+  if (f32_ok(p)) return p->D == 64 ? launch_f32<64>(sp, p, s) : launch_f32<32>(sp, p, s);
   switch (p->in_dtype) {
     case CEA_F64:
       return launch_simt_d<double, double, double>(sp, p, s);

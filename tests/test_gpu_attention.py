@@ -274,6 +274,46 @@ def test_simt_vs_oracle(dtype):
     _cmp(_np(l), ref_l, ltol)
 
 
+@pytest.mark.parametrize(
+    "B,Sq,Sk,Hq,Hkv,D,causal,pad,q_off",
+    [
+        (1, 2048, 2048, 8, 8, 64, True, 0, None),   # config 1 at SP=1
+        (2, 100, 300, 6, 2, 64, True, 11, None),    # GQA, ragged tiles, padded keys
+        (1, 70, 130, 4, 1, 32, False, 0, None),     # MQA, non-causal, D=32
+        (1, 33, 513, 2, 2, 64, True, 0, 1000),      # queries past every key: all visible
+        (1, 64, 200, 2, 1, 64, True, 0, -100),      # queries before every key: empty rows
+    ],
+)
+def test_f32_kernel_vs_oracle(B, Sq, Sk, Hq, Hkv, D, causal, pad, q_off):
+    # fp32 with head dim 32/64 runs the register-tiled CUDA-core kernel (kind 3); 1e-4 out / 1e-5 lse
+    q, k, v, qp, kp = _inputs(B, Sq, Sk, Hq, Hkv, D, torch.float32, seed=Sq + Sk, pad=pad, q_off=q_off)
+    ref_o, ref_l = _oracle(q, k, v, qp, kp, causal)
+    qd, kd, vd, qpd, kpd = (t.to(DEV) for t in (q, k, v, qp, kp))
+    out = torch.empty(B, Sq, Hq, D, dtype=torch.float32, device=DEV)
+    lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=DEV)
+    assert _kind(qd, kd, vd, qpd, kpd, out, lse, causal=causal) == _lib.KIND_SIMT
+    cea.attend_into(qd, kd, vd, qpd, kpd, out, lse, causal=causal)
+    _cmp(_np(out), ref_o, 1e-4)
+    _cmp(_np(lse), ref_l, 1e-5)
+    # the same keys in two halves merged by the epilogue (a ring step), with a kv_map naming the KV heads
+    kv_map = [h * Hkv // Hq for h in range(Hq)]
+    half = Sk // 2
+    cea.attend_into(qd, kd[:, half:], vd[:, half:], qpd, kpd[:, half:], out, lse, causal=causal, kv_map=kv_map)
+    cea.attend_into(qd, kd[:, :half], vd[:, :half], qpd, kpd[:, :half], out, lse, causal=causal, kv_map=kv_map,
+                    accumulate=True)
+    _cmp(_np(out), ref_o, 1e-4)
+    _cmp(_np(lse), ref_l, 1e-5)
+
+
+def test_f32_generic_head_dim_vs_oracle():
+    # fp32 at a head dim the register-tiled kernel does not take (48) stays on the generic CUDA-core kernel
+    q, k, v, qp, kp = _inputs(1, 90, 150, 4, 2, 48, torch.float32, seed=4, pad=7)
+    ref_o, ref_l = _oracle(q, k, v, qp, kp, True)
+    o, l = cea.attention_with_lse(q.to(DEV), k.to(DEV), v.to(DEV), qp.to(DEV), kp.to(DEV))
+    _cmp(_np(o), ref_o, 1e-4)
+    _cmp(_np(l), ref_l, 1e-5)
+
+
 # ----------------------------------------------------------------------------- split-KV decode
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,Sq,Hq,Hkv,D,T", [(2, 1, 8, 2, 128, 5000), (3, 2, 8, 2, 64, 777), (1, 1, 4, 4, 128, 64)])
