@@ -1,13 +1,13 @@
 // fp32 attention with log-sum-exp for head dims 32 and 64 on the CUDA cores (collab_infer's config-1 precision: out
 // within 1e-4 and lse within 1e-5 of the reference's fp32 computation, parallel/attention.py:163-181).
 //
-// CTA = 32 query rows of one head x 4 threads per row (128 threads).  Each thread keeps its row of q (pre-loaded,
-// D registers) and a full D-wide output accumulator, and runs its own online softmax over every 4th key of each
-// 64-key block (keys u, u+4, ... for thread u): the dot products and the P.V update then need no exchange inside
-// the loop, and the four partial (m, l, o) of a row are merged exactly once at the end (shuffles).  K/V blocks are
-// staged in shared memory by cp.async, two stages, rows padded to D + 4 floats so that the 16-byte reads of the four
-// keys a warp touches at once fall in distinct banks.  Only the key blocks a CTA can see are loaded: a pre-pass over
-// the key positions gives the first and last block holding a visible key for any of the CTA's rows.
+// CTA = 16 query rows of one head x 8 threads per row (128 threads).  Thread u of a row keeps the row of q in
+// registers, scores keys u, u+8, ... of each 32-key block (whole dot products, no exchange), and owns D/8 of the
+// row's output columns (32c + 4u + e): the eight threads share the row's running max (three shuffles per block),
+// pass their probabilities through a small shared-memory row, and each updates only its output columns.  K/V
+// blocks are staged in shared memory by cp.async, two stages, rows padded to D + 4 floats so that the 16-byte
+// reads of a warp fall in distinct banks.  Only the key blocks a CTA can see are loaded: a pre-pass over the key
+// positions gives the first and last block holding a visible key for any of the CTA's rows.
 #pragma once
 
 #include "cea_common.cuh"
@@ -16,17 +16,18 @@
 namespace cea {
 namespace f32k {
 
-constexpr int ROWS = 32;         // query rows per CTA
-constexpr int TPR = 4;           // threads per row
+constexpr int ROWS = 16;         // query rows per CTA
+constexpr int TPR = 8;           // threads per row
 constexpr int NT = ROWS * TPR;   // 128
-constexpr int BK = 64;           // keys per staged block
+constexpr int BK = 32;           // keys per staged block
 constexpr int KPT = BK / TPR;    // keys per thread per block
 constexpr int STAGES = 2;
 template <int D>
 struct Smem {
   static constexpr int KSTR = D + 4;  // padded row stride of the staged K/V blocks (floats)
   static constexpr int KV = STAGES * BK * KSTR;  // floats per tensor
-  static constexpr size_t BYTES = 2 * KV * sizeof(float) + STAGES * BK * sizeof(long long);
+  static constexpr int PSTR = BK + 8;  // probability row stride (floats): the 4 rows of a warp in distinct banks
+  static constexpr size_t BYTES = 2 * KV * sizeof(float) + ROWS * PSTR * sizeof(float) + STAGES * BK * sizeof(long long);
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool in) {
@@ -40,18 +41,21 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // simt::Params carries the same operands (element strides); p.D == D
 template <int D>
-__global__ void __launch_bounds__(NT, 3) attn_f32_kernel(const simt::Params p) {
+__global__ void __launch_bounds__(NT, 4) attn_f32_kernel(const simt::Params p) {
   constexpr int KSTR = Smem<D>::KSTR;
+  constexpr int PSTR = Smem<D>::PSTR;
+  constexpr int OC = D / TPR;  // output columns per thread
   extern __shared__ __align__(16) uint8_t smem_raw[];
   float* Ks = reinterpret_cast<float*>(smem_raw);
   float* Vs = Ks + Smem<D>::KV;
-  long long* kps = reinterpret_cast<long long*>(Vs + Smem<D>::KV);
+  float* Ps = Vs + Smem<D>::KV;  // [ROWS][PSTR]
+  long long* kps = reinterpret_cast<long long*>(Ps + ROWS * PSTR);
   __shared__ int s_range[2];
   __shared__ long long s_qmax;
 
   const int t = threadIdx.x;
-  const int r = t >> 2;
-  const int u = t & 3;
+  const int r = t / TPR;
+  const int u = t % TPR;
   const int b = blockIdx.z;
   const int h = blockIdx.y;
   const int nblk = gridDim.x;
@@ -103,9 +107,10 @@ __global__ void __launch_bounds__(NT, 3) attn_f32_kernel(const simt::Params p) {
 #pragma unroll
     for (int d = 0; d < D; ++d) q[d] = row_in ? qg[d] : 0.f;
   }
-  float o[D];
+  float o[OC];  // o[4c + e] is output column 4 TPR c + 4u + e
 #pragma unroll
-  for (int d = 0; d < D; ++d) o[d] = 0.f;
+  for (int d = 0; d < OC; ++d) o[d] = 0.f;
+  float* prow = Ps + r * PSTR;
   float m = -INFINITY, l = 0.f;
   const float scale = static_cast<float>(p.scale);
 
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(NT, 3) attn_f32_kernel(const simt::Params p) {
     const float* Vb = Vs + st * BK * KSTR;
     const long long* kpb = kps + st * BK;
 
-    // scores of this thread's 16 keys (u, u+4, ...), 16-byte reads of K rows
+    // scores of this thread's keys (u, u+4, ...), 16-byte reads of K rows
     float s[KPT];
 #pragma unroll
     for (int i = 0; i < KPT; ++i) s[i] = 0.f;
@@ -170,50 +175,53 @@ __global__ void __launch_bounds__(NT, 3) attn_f32_kernel(const simt::Params p) {
       s[i] = vis ? s[i] * scale : -INFINITY;
       mb = fmaxf(mb, s[i]);
     }
+    // the row's max over its four threads: the row's probabilities then share one reference
+#pragma unroll
+    for (int off = 1; off < TPR; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
     const float m_new = fmaxf(m, mb);
-    if (m_new != -INFINITY) {  // this thread's keys of the block are not all masked
+    const bool any = m_new != -INFINITY;  // the same for the four threads of a row
+    if (any) {
       const float alpha = expf(m - m_new);  // 0 while nothing has been seen
       float rs = 0.f;
 #pragma unroll
       for (int i = 0; i < KPT; ++i) {
         s[i] = expf(s[i] - m_new);
         rs += s[i];
+        prow[i * TPR + u] = s[i];
       }
-      l = l * alpha + rs;
+      l = l * alpha + rs;  // this thread's part of the row sum; the parts are added at the end
       m = m_new;
 #pragma unroll
-      for (int d = 0; d < D; ++d) o[d] *= alpha;
+      for (int d = 0; d < OC; ++d) o[d] *= alpha;
+    }
+    __syncwarp();
+    if (any) {
+      // every key of the block, this thread's output columns 4 TPR c + 4u + e
 #pragma unroll
-      for (int i = 0; i < KPT; ++i) {
-        const float pi = s[i];
+      for (int j4 = 0; j4 < BK / 4; ++j4) {
+        const float4 p4 = *reinterpret_cast<const float4*>(prow + 4 * j4);
+        const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
-        for (int d4 = 0; d4 < D / 4; ++d4) {
-          const float4 vv = *reinterpret_cast<const float4*>(Vb + (i * TPR + u) * KSTR + d4 * 4);
-          o[d4 * 4 + 0] = fmaf(pi, vv.x, o[d4 * 4 + 0]);
-          o[d4 * 4 + 1] = fmaf(pi, vv.y, o[d4 * 4 + 1]);
-          o[d4 * 4 + 2] = fmaf(pi, vv.z, o[d4 * 4 + 2]);
-          o[d4 * 4 + 3] = fmaf(pi, vv.w, o[d4 * 4 + 3]);
+        for (int jj = 0; jj < 4; ++jj) {
+          const float* vrow = Vb + (4 * j4 + jj) * KSTR + 4 * u;
+#pragma unroll
+          for (int c = 0; c < OC / 4; ++c) {
+            const float4 vv = *reinterpret_cast<const float4*>(vrow + 4 * TPR * c);
+            o[4 * c + 0] = fmaf(pj[jj], vv.x, o[4 * c + 0]);
+            o[4 * c + 1] = fmaf(pj[jj], vv.y, o[4 * c + 1]);
+            o[4 * c + 2] = fmaf(pj[jj], vv.z, o[4 * c + 2]);
+            o[4 * c + 3] = fmaf(pj[jj], vv.w, o[4 * c + 3]);
+          }
         }
       }
     }
     __syncthreads();  // the stage is overwritten by the load issued in the next iteration
   }
 
-  // ---- exact merge of the row's four partial softmaxes (lanes 4r .. 4r+3 of one warp)
-  float M = m;
-#pragma unroll
-  for (int off = 1; off < TPR; off <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  const float w = (m == -INFINITY) ? 0.f : expf(m - M);
-  l *= w;
+  // ---- the row sum: the four threads' parts, scaled alike
 #pragma unroll
   for (int off = 1; off < TPR; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-#pragma unroll
-  for (int d = 0; d < D; ++d) {
-    float x = o[d] * w;
-#pragma unroll
-    for (int off = 1; off < TPR; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
-    o[d] = x;
-  }
+  const float M = m;
   if (!row_in) return;
 
   const float lse_row = l > 0.f ? M + logf(l) : -INFINITY;
@@ -234,17 +242,15 @@ __global__ void __launch_bounds__(NT, 3) attn_f32_kernel(const simt::Params p) {
     }
   }
   float* og = reinterpret_cast<float*>(p.out) + b * p.o_sb + static_cast<int64_t>(qi) * p.o_ss + h * p.o_sh;
-  // thread u writes columns [u D/4, (u + 1) D/4); a constant-index select keeps o in registers
 #pragma unroll
-  for (int dd = 0; dd < D / TPR; ++dd) {
-    float val = 0.f;
+  for (int c = 0; c < OC / 4; ++c) {
 #pragma unroll
-    for (int uu = 0; uu < TPR; ++uu)
-      if (uu == u) val = o[uu * (D / TPR) + dd];
-    val = val * inv_l * w_new;
-    const int d = u * (D / TPR) + dd;
-    if (p.accumulate) val += og[d] * w_old;
-    og[d] = val;
+    for (int e = 0; e < 4; ++e) {
+      const int d = 4 * TPR * c + 4 * u + e;
+      float val = o[4 * c + e] * inv_l * w_new;
+      if (p.accumulate) val += og[d] * w_old;
+      og[d] = val;
+    }
   }
   if (u == 0 && lse_ptr) *lse_ptr = lse_out;
 }
