@@ -1,13 +1,17 @@
 // fp32 attention with log-sum-exp for head dims 32 and 64 on the CUDA cores (collab_infer's config-1 precision: out
 // within 1e-4 and lse within 1e-5 of the reference's fp32 computation, parallel/attention.py:163-181).
 //
-// CTA = 16 query rows of one head x 8 threads per row (128 threads).  Thread u of a row keeps the row of q in
-// registers, scores keys u, u+8, ... of each 32-key block (whole dot products, no exchange), and owns D/8 of the
-// row's output columns (32c + 4u + e): the eight threads share the row's running max (three shuffles per block),
-// pass their probabilities through a small shared-memory row, and each updates only its output columns.  K/V
-// blocks are staged in shared memory by cp.async, two stages, rows padded to D + 4 floats so that the 16-byte
-// reads of a warp fall in distinct banks.  Only the key blocks a CTA can see are loaded: a pre-pass over the key
-// positions gives the first and last block holding a visible key for any of the CTA's rows.
+// Register-tiled like a CUDA-core GEMM: a CTA (128 threads) owns 64-row blocks of one head's queries and walks
+// 64-key blocks staged in shared memory.  Under a causal mask the row blocks see very different key counts, so a
+// CTA takes two of them, the i-th from each end of the sequence, and every CTA has about the same work (the longest
+// CTA otherwise sets the launch's duration).  Thread (tr, tk) (tr = 0..15, tk = 0..7, the 8 tk of a tr in one warp) holds the scores
+// of rows tr + 16i (i = 0..3) against keys tk + 8j (j = 0..7) and the output of the same rows at columns
+// 4tk + 32c + e: each 16-byte shared-memory read then feeds 8 (scores) or 10.7 (output) FMAs on average instead of
+// 4, which is what bounds an untiled kernel (shared-memory wavefronts).  Per block: S = Q K^T into registers, the
+// position mask, the row max over the 8 threads of a row (shuffles), P = exp(S - m) into a transposed shared row
+// buffer (rows of a thread contiguous), O = O alpha + P V.  Each thread keeps a partial row sum; the 8 parts share
+// the row's max sequence and are added once at the end.  K/V blocks arrive by cp.async, two stages; only the
+// key blocks a CTA can see are loaded (a pre-pass over the key positions gives the first and last one).
 #pragma once
 
 #include "cea_common.cuh"
@@ -16,18 +20,26 @@
 namespace cea {
 namespace f32k {
 
-constexpr int ROWS = 16;         // query rows per CTA
-constexpr int TPR = 8;           // threads per row
-constexpr int NT = ROWS * TPR;   // 128
-constexpr int BK = 32;           // keys per staged block
-constexpr int KPT = BK / TPR;    // keys per thread per block
+constexpr int ROWS = 64;   // query rows per CTA
+constexpr int NT = 128;    // threads: 16 row groups x 8 key / column groups
+constexpr int BK = 64;     // keys per staged block
+constexpr int RI = 4;      // rows per thread (tr + 16 i)
+constexpr int KJ = 8;      // keys per thread per block (tk + 8 j)
 constexpr int STAGES = 2;
+// CTAs along the query axis: under a causal mask two 64-row blocks each (the middle block alone when their count
+// is odd), else one
+__host__ __device__ constexpr int grid_x(int Sq, bool causal) {
+  return causal ? ((Sq + ROWS - 1) / ROWS + 1) / 2 : (Sq + ROWS - 1) / ROWS;
+}
+
 template <int D>
 struct Smem {
-  static constexpr int KSTR = D + 4;  // padded row stride of the staged K/V blocks (floats)
-  static constexpr int KV = STAGES * BK * KSTR;  // floats per tensor
-  static constexpr int PSTR = BK + 8;  // probability row stride (floats): the 4 rows of a warp in distinct banks
-  static constexpr size_t BYTES = 2 * KV * sizeof(float) + ROWS * PSTR * sizeof(float) + STAGES * BK * sizeof(long long);
+  static constexpr int STR = D + 4;               // padded row stride of Q, K, V (floats)
+  static constexpr int PSTR = 4 * 16 + 4;         // transposed probabilities: [key][4 tr + i]
+  static constexpr int Q = ROWS * STR;            // floats
+  static constexpr int KV = STAGES * BK * STR;    // floats per tensor
+  static constexpr int P = BK * PSTR;
+  static constexpr size_t BYTES = (Q + 2 * KV + P) * sizeof(float) + STAGES * BK * sizeof(long long);
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool in) {
@@ -41,40 +53,59 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // simt::Params carries the same operands (element strides); p.D == D
 template <int D>
-__global__ void __launch_bounds__(NT, 4) attn_f32_kernel(const simt::Params p) {
-  constexpr int KSTR = Smem<D>::KSTR;
-  constexpr int PSTR = Smem<D>::PSTR;
-  constexpr int OC = D / TPR;  // output columns per thread
+__global__ void __launch_bounds__(NT, 2) attn_f32_kernel(const simt::Params p) {
+  using S = Smem<D>;
+  constexpr int STR = S::STR;
+  constexpr int PSTR = S::PSTR;
+  constexpr int DC = D / 32;  // 4-column groups per thread: columns 4 tk + 32 c + e
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  float* Ks = reinterpret_cast<float*>(smem_raw);
-  float* Vs = Ks + Smem<D>::KV;
-  float* Ps = Vs + Smem<D>::KV;  // [ROWS][PSTR]
-  long long* kps = reinterpret_cast<long long*>(Ps + ROWS * PSTR);
+  float* Qs = reinterpret_cast<float*>(smem_raw);  // [ROWS][STR], rows in query order
+  float* Ks = Qs + S::Q;
+  float* Vs = Ks + S::KV;
+  float* Pt = Vs + S::KV;  // [BK][PSTR]: probability of key j for row tr + 16 i at j * PSTR + 4 tr + i
+  long long* kps = reinterpret_cast<long long*>(Pt + S::P);
   __shared__ int s_range[2];
   __shared__ long long s_qmax;
 
   const int t = threadIdx.x;
-  const int r = t / TPR;
-  const int u = t % TPR;
+  const int lane = t & 31;
+  const int tk = lane & 7;
+  const int tr = (t >> 5) * 4 + (lane >> 3);
   const int b = blockIdx.z;
   const int h = blockIdx.y;
-  const int nblk = gridDim.x;
-  const int q0 = (nblk - 1 - static_cast<int>(blockIdx.x)) * ROWS;  // the rows with the most keys start first
   const int kvh = p.kv_map ? p.kv_map[h] : h / p.group;
   const bool causal = p.causal != 0;
+  const int nblk = (p.Sq + ROWS - 1) / ROWS;
+  const int near = static_cast<int>(blockIdx.x);
+  const int far = causal ? nblk - 1 - near : near;
 
-  const int qi = q0 + r;
-  const bool row_in = qi < p.Sq;
-  const long long qpos = row_in ? p.q_pos[b * p.qpos_sb + static_cast<int64_t>(qi) * p.qpos_ss] : -1ll;
+  for (int pass = 0; pass < 2; ++pass) {
+  if (pass == 1 && near == far) break;
+  const int q0 = (pass == 0 ? far : near) * ROWS;
+
+  // ---- this thread's rows and their positions
+  long long qpos[RI];
+#pragma unroll
+  for (int i = 0; i < RI; ++i) {
+    const int qi = q0 + tr + 16 * i;
+    qpos[i] = qi < p.Sq ? p.q_pos[b * p.qpos_sb + static_cast<int64_t>(qi) * p.qpos_ss] : -1ll;
+  }
 
   // ---- the CTA's visible key blocks: [first, last] over keys with 0 <= kpos (<= max q position when causal)
+  __syncthreads();  // the previous row block's readers of the shared state are done
   if (t == 0) {
     s_range[0] = INT_MAX;
     s_range[1] = -1;
     s_qmax = -1;
   }
   __syncthreads();
-  if (u == 0 && row_in) atomicMax(&s_qmax, qpos);
+  if (tk == 0) {
+    long long mx = -1;
+#pragma unroll
+    for (int i = 0; i < RI; ++i)
+      if (q0 + tr + 16 * i < p.Sq) mx = max(mx, qpos[i]);
+    atomicMax(&s_qmax, mx);
+  }
   __syncthreads();
   const long long qmax = s_qmax;
   {
@@ -92,42 +123,49 @@ __global__ void __launch_bounds__(NT, 4) attn_f32_kernel(const simt::Params p) {
       first = min(first, __shfl_xor_sync(0xffffffffu, first, off));
       last = max(last, __shfl_xor_sync(0xffffffffu, last, off));
     }
-    if ((t & 31) == 0) {
+    if (lane == 0) {
       atomicMin(&s_range[0], first);
       atomicMax(&s_range[1], last);
+    }
+  }
+
+  // ---- the CTA's query rows into shared memory (zero past Sq)
+  {
+    const float* qg = reinterpret_cast<const float*>(p.q) + b * p.q_sb + h * p.q_sh;
+    for (int e = t; e < ROWS * D; e += NT) {
+      const int row = e / D, d = e % D;
+      const int qi = q0 + row;
+      Qs[row * STR + d] = qi < p.Sq ? qg[static_cast<int64_t>(qi) * p.q_ss + d] : 0.f;
     }
   }
   __syncthreads();
   const int kb0 = s_range[0], kb1 = s_range[1];
 
-  // ---- q row into registers
-  float q[D];
-  {
-    const float* qg = reinterpret_cast<const float*>(p.q) + b * p.q_sb + h * p.q_sh + static_cast<int64_t>(qi) * p.q_ss;
+  float o[RI][4 * DC];  // o[i][4c + e]: row tr + 16 i, column 4 tk + 32 c + e
+  float m[RI], l[RI];
 #pragma unroll
-    for (int d = 0; d < D; ++d) q[d] = row_in ? qg[d] : 0.f;
+  for (int i = 0; i < RI; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int d = 0; d < 4 * DC; ++d) o[i][d] = 0.f;
   }
-  float o[OC];  // o[4c + e] is output column 4 TPR c + 4u + e
-#pragma unroll
-  for (int d = 0; d < OC; ++d) o[d] = 0.f;
-  float* prow = Ps + r * PSTR;
-  float m = -INFINITY, l = 0.f;
   const float scale = static_cast<float>(p.scale);
 
   const float* kg = reinterpret_cast<const float*>(p.k) + b * p.k_sb + kvh * p.k_sh;
   const float* vg = reinterpret_cast<const float*>(p.v) + b * p.v_sb + kvh * p.v_sh;
   const int64_t* kpg = p.k_pos + b * p.kpos_sb;
-  // block kb into stage st: 64 rows x D/4 chunks of 16 bytes for K and for V; positions by 64 threads
+  // block kb into stage st: BK rows x D/4 chunks of 16 bytes for K and for V; positions by BK threads
   auto load_block = [&](int kb, int st) {
-    const uint32_t ks = smem_u32(Ks + st * BK * KSTR), vs = smem_u32(Vs + st * BK * KSTR);
+    const uint32_t ks = smem_u32(Ks + st * BK * STR), vs = smem_u32(Vs + st * BK * STR);
 #pragma unroll
-    for (int i = 0; i < (BK * D / 4) / NT; ++i) {
-      const int c = t + i * NT;  // chunk: key row c / (D/4), 4-float column group c % (D/4)
+    for (int it = 0; it < (BK * D / 4) / NT; ++it) {
+      const int c = t + it * NT;  // chunk: key row c / (D/4), 4-float column group c % (D/4)
       const int row = c / (D / 4), col = (c % (D / 4)) * 4;
       const int kj = kb * BK + row;
       const bool in = kj < p.Sk;
       const int64_t kjs = in ? kj : 0;
-      const uint32_t so = static_cast<uint32_t>((row * KSTR + col) * sizeof(float));
+      const uint32_t so = static_cast<uint32_t>((row * STR + col) * sizeof(float));
       cp_async16(ks + so, kg + kjs * p.k_ss + col, in);
       cp_async16(vs + so, vg + kjs * p.v_ss + col, in);
     }
@@ -148,111 +186,123 @@ __global__ void __launch_bounds__(NT, 4) attn_f32_kernel(const simt::Params p) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const float* Kb = Ks + st * BK * KSTR;
-    const float* Vb = Vs + st * BK * KSTR;
+    const float* Kb = Ks + st * BK * STR;
+    const float* Vb = Vs + st * BK * STR;
     const long long* kpb = kps + st * BK;
 
-    // scores of this thread's keys (u, u+4, ...), 16-byte reads of K rows
-    float s[KPT];
+    // S tile: rows tr + 16 i, keys tk + 8 j
+    float s[RI][KJ];
 #pragma unroll
-    for (int i = 0; i < KPT; ++i) s[i] = 0.f;
+    for (int i = 0; i < RI; ++i)
 #pragma unroll
+      for (int j = 0; j < KJ; ++j) s[i][j] = 0.f;
+#pragma unroll 4
     for (int d4 = 0; d4 < D / 4; ++d4) {
+      float4 qv[RI], kv[KJ];
 #pragma unroll
-      for (int i = 0; i < KPT; ++i) {
-        const float4 kv = *reinterpret_cast<const float4*>(Kb + (i * TPR + u) * KSTR + d4 * 4);
-        s[i] = fmaf(q[d4 * 4 + 0], kv.x, s[i]);
-        s[i] = fmaf(q[d4 * 4 + 1], kv.y, s[i]);
-        s[i] = fmaf(q[d4 * 4 + 2], kv.z, s[i]);
-        s[i] = fmaf(q[d4 * 4 + 3], kv.w, s[i]);
+      for (int i = 0; i < RI; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (tr + 16 * i) * STR + 4 * d4);
+#pragma unroll
+      for (int j = 0; j < KJ; ++j) kv[j] = *reinterpret_cast<const float4*>(Kb + (tk + 8 * j) * STR + 4 * d4);
+#pragma unroll
+      for (int i = 0; i < RI; ++i)
+#pragma unroll
+        for (int j = 0; j < KJ; ++j) {
+          s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+          s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+          s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+          s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+        }
+    }
+
+    // mask, the row max over the row's 8 threads, probabilities into the transposed row buffer
+    long long kp[KJ];
+#pragma unroll
+    for (int j = 0; j < KJ; ++j) kp[j] = kpb[tk + 8 * j];
+#pragma unroll
+    for (int i = 0; i < RI; ++i) {
+      float mb = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < KJ; ++j) {
+        const bool vis = kp[j] >= 0 && (!causal || kp[j] <= qpos[i]);
+        s[i][j] = vis ? s[i][j] * scale : -INFINITY;
+        mb = fmaxf(mb, s[i][j]);
       }
-    }
-    float mb = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < KPT; ++i) {
-      const long long kp = kpb[i * TPR + u];
-      const bool vis = kp >= 0 && (!causal || kp <= qpos);
-      s[i] = vis ? s[i] * scale : -INFINITY;
-      mb = fmaxf(mb, s[i]);
-    }
-    // the row's max over its four threads: the row's probabilities then share one reference
-#pragma unroll
-    for (int off = 1; off < TPR; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-    const float m_new = fmaxf(m, mb);
-    const bool any = m_new != -INFINITY;  // the same for the four threads of a row
-    if (any) {
-      const float alpha = expf(m - m_new);  // 0 while nothing has been seen
+      for (int off = 1; off < 8; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+      const float m_new = fmaxf(m[i], mb);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row that has seen nothing keeps p = 0
+      const float alpha = expf(m[i] - m_use);                 // 0 while the row has seen nothing
+      m[i] = m_new;
       float rs = 0.f;
 #pragma unroll
-      for (int i = 0; i < KPT; ++i) {
-        s[i] = expf(s[i] - m_new);
-        rs += s[i];
-        prow[i * TPR + u] = s[i];
+      for (int j = 0; j < KJ; ++j) {
+        const float pj = expf(s[i][j] - m_use);
+        rs += pj;
+        Pt[(tk + 8 * j) * PSTR + 4 * tr + i] = pj;
       }
-      l = l * alpha + rs;  // this thread's part of the row sum; the parts are added at the end
-      m = m_new;
+      l[i] = l[i] * alpha + rs;  // this thread's part of the row sum
 #pragma unroll
-      for (int d = 0; d < OC; ++d) o[d] *= alpha;
+      for (int d = 0; d < 4 * DC; ++d) o[i][d] *= alpha;
     }
-    __syncwarp();
-    if (any) {
-      // every key of the block, this thread's output columns 4 TPR c + 4u + e
+    __syncwarp();  // a row's probabilities come from the 8 threads of its row group, all in this warp
+
+    // O += P V over the block's keys: 4 probabilities (one 16-byte read) x 4 DC columns per key
+#pragma unroll 4
+    for (int j = 0; j < BK; ++j) {
+      const float4 pv = *reinterpret_cast<const float4*>(Pt + j * PSTR + 4 * tr);
+      const float pr[RI] = {pv.x, pv.y, pv.z, pv.w};
 #pragma unroll
-      for (int j4 = 0; j4 < BK / 4; ++j4) {
-        const float4 p4 = *reinterpret_cast<const float4*>(prow + 4 * j4);
-        const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+      for (int c = 0; c < DC; ++c) {
+        const float4 vv = *reinterpret_cast<const float4*>(Vb + j * STR + 4 * tk + 32 * c);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const float* vrow = Vb + (4 * j4 + jj) * KSTR + 4 * u;
-#pragma unroll
-          for (int c = 0; c < OC / 4; ++c) {
-            const float4 vv = *reinterpret_cast<const float4*>(vrow + 4 * TPR * c);
-            o[4 * c + 0] = fmaf(pj[jj], vv.x, o[4 * c + 0]);
-            o[4 * c + 1] = fmaf(pj[jj], vv.y, o[4 * c + 1]);
-            o[4 * c + 2] = fmaf(pj[jj], vv.z, o[4 * c + 2]);
-            o[4 * c + 3] = fmaf(pj[jj], vv.w, o[4 * c + 3]);
-          }
+        for (int i = 0; i < RI; ++i) {
+          o[i][4 * c + 0] = fmaf(pr[i], vv.x, o[i][4 * c + 0]);
+          o[i][4 * c + 1] = fmaf(pr[i], vv.y, o[i][4 * c + 1]);
+          o[i][4 * c + 2] = fmaf(pr[i], vv.z, o[i][4 * c + 2]);
+          o[i][4 * c + 3] = fmaf(pr[i], vv.w, o[i][4 * c + 3]);
         }
       }
     }
-    __syncthreads();  // the stage is overwritten by the load issued in the next iteration
+    __syncthreads();  // the stage and the row buffer are rewritten in the next iteration
   }
 
-  // ---- the row sum: the four threads' parts, scaled alike
+  // ---- epilogue: the row sums (8 parts, same max sequence), normalisation, the optional exact merge
 #pragma unroll
-  for (int off = 1; off < TPR; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-  const float M = m;
-  if (!row_in) return;
-
-  const float lse_row = l > 0.f ? M + logf(l) : -INFINITY;
-  const float inv_l = l > 0.f ? 1.f / l : 0.f;
-  float w_old = 0.f, w_new = 1.f, lse_out = lse_row;
-  float* lse_ptr = p.lse ? reinterpret_cast<float*>(p.lse) + b * p.l_sb + h * p.l_sh + static_cast<int64_t>(qi) * p.l_ss
-                         : nullptr;
-  if (p.accumulate) {
-    const float lse_old = *lse_ptr;
-    const float mx = fmaxf(lse_old, lse_row);
-    if (mx == -INFINITY) {
-      lse_out = -INFINITY;
-      w_new = 0.f;
-    } else {
-      lse_out = mx + log1pf(expf(-fabsf(lse_old - lse_row)));
-      w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - lse_out);
-      w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - lse_out);
+  for (int i = 0; i < RI; ++i) {
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], off);
+    const int qi = q0 + tr + 16 * i;
+    if (qi >= p.Sq) continue;
+    const float lse_row = l[i] > 0.f ? m[i] + logf(l[i]) : -INFINITY;
+    const float inv_l = l[i] > 0.f ? 1.f / l[i] : 0.f;
+    float w_old = 0.f, w_new = 1.f, lse_out = lse_row;
+    float* lse_ptr = p.lse ? reinterpret_cast<float*>(p.lse) + b * p.l_sb + h * p.l_sh + static_cast<int64_t>(qi) * p.l_ss
+                           : nullptr;
+    if (p.accumulate) {
+      const float lse_old = *lse_ptr;
+      const float mx = fmaxf(lse_old, lse_row);
+      if (mx == -INFINITY) {
+        lse_out = -INFINITY;
+        w_new = 0.f;
+      } else {
+        lse_out = mx + log1pf(expf(-fabsf(lse_old - lse_row)));
+        w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - lse_out);
+        w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - lse_out);
+      }
     }
-  }
-  float* og = reinterpret_cast<float*>(p.out) + b * p.o_sb + static_cast<int64_t>(qi) * p.o_ss + h * p.o_sh;
+    float* og = reinterpret_cast<float*>(p.out) + b * p.o_sb + static_cast<int64_t>(qi) * p.o_ss + h * p.o_sh;
 #pragma unroll
-  for (int c = 0; c < OC / 4; ++c) {
+    for (int c = 0; c < DC; ++c)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = 4 * TPR * c + 4 * u + e;
-      float val = o[4 * c + e] * inv_l * w_new;
-      if (p.accumulate) val += og[d] * w_old;
-      og[d] = val;
-    }
+      for (int e = 0; e < 4; ++e) {
+        const int d = 4 * tk + 32 * c + e;
+        float val = o[i][4 * c + e] * inv_l * w_new;
+        if (p.accumulate) val += og[d] * w_old;
+        og[d] = val;
+      }
+    if (tk == 0 && lse_ptr) *lse_ptr = lse_out;
   }
-  if (u == 0 && lse_ptr) *lse_ptr = lse_out;
+  }  // row blocks
 }
 
 }  // namespace f32k

@@ -484,7 +484,7 @@ template <int DD>
 int launch_f32(const simt::Params& sp, const cea_attn_params* p, cudaStream_t s) {
   auto k = f32k::attn_f32_kernel<DD>;
   allow_smem(k, static_cast<int>(f32k::Smem<DD>::BYTES));
-  const dim3 grid((p->Sq + f32k::ROWS - 1) / f32k::ROWS, p->Hq, p->B);
+  const dim3 grid(f32k::grid_x(p->Sq, p->causal != 0), p->Hq, p->B);
   k<<<grid, f32k::NT, f32k::Smem<DD>::BYTES, s>>>(sp);
   return cuda_check("attn_f32_kernel");
 }
