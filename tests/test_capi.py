@@ -47,6 +47,27 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.cea_ulysses_pack(ctypes.byref(c), None) == _lib.CEA_ERR_INVALID
 
 
+def test_acc_in_rules_are_checked_without_a_gpu():
+    # acc_in (the ring's last step merging from an fp32 running result into a 16-bit out) is refused where it
+    # cannot apply; every check here returns before any CUDA call
+    lib = _lib.load()
+    fake = 1 << 20  # never dereferenced: validation fails first
+    p = _lib.AttnParams()
+    p.B, p.Sq, p.Sk, p.Hq, p.Hkv, p.D = 1, 4, 4, 2, 2, 64
+    p.q = p.k = p.v = p.out = p.lse = p.q_pos = p.k_pos = p.acc_in = fake
+    p.in_dtype = _lib.BF16
+    p.out_dtype, p.accumulate = _lib.F32, 1  # a wide out needs no acc_in
+    assert lib.cea_attn_fwd(ctypes.byref(p), None) == _lib.CEA_ERR_INVALID
+    assert b"16-bit output" in lib.cea_last_error()
+    p.out_dtype, p.accumulate = _lib.BF16, 0  # acc_in is the running result of an accumulating call
+    assert lib.cea_attn_fwd(ctypes.byref(p), None) == _lib.CEA_ERR_INVALID
+    p.accumulate, p.Sk = 1, 0  # nothing to merge
+    assert lib.cea_attn_fwd(ctypes.byref(p), None) == _lib.CEA_ERR_UNSUPPORTED
+    assert b"no keys" in lib.cea_last_error()
+    p.acc_in, p.Sk = None, 4  # accumulate into a 16-bit out without acc_in
+    assert lib.cea_attn_fwd(ctypes.byref(p), None) == _lib.CEA_ERR_INVALID
+
+
 def test_nccl_entry_points_reject_bad_arguments_without_nccl_or_gpu():
     lib = _lib.load()
     P = ctypes.c_void_p
