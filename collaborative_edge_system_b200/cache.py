@@ -116,21 +116,29 @@ class LayerKVCache:
     def view(
         self, like_k: Optional[torch.Tensor] = None, like_pos: Optional[torch.Tensor] = None
     ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """Cached ``(k, v, pos)`` as token-major views; empty tensors shaped like ``like_*`` if unused."""
-        if self.k is None:
-            if like_k is None or like_pos is None:
-                raise RuntimeError("empty cache: provide templates to build empty views")
-            empty = like_k.new_empty((like_k.shape[0], 0) + tuple(like_k.shape[2:]))
-            return empty, empty, like_pos.new_empty((like_pos.shape[0], 0))
-        n = self.length
-        return self.k[:, :, :n].transpose(1, 2), self.v[:, :, :n].transpose(1, 2), self.pos[:, :n]
+        """The ``length`` cached tokens as token-major views ``k``/``v`` ``[B, T, H, D]`` and ``pos`` ``[B, T]`` of the
+        head-major storage (no copy).  Before the first append there is no storage: the views are zero-length
+        tensors shaped after the ``like_k`` / ``like_pos`` templates, which must then be given."""
+        if self.k is not None:
+            t = self.length
+            return (self.k.narrow(2, 0, t).transpose(1, 2), self.v.narrow(2, 0, t).transpose(1, 2),
+                    self.pos.narrow(1, 0, t))
+        if like_k is None or like_pos is None:
+            raise RuntimeError("the cache holds no tokens yet: pass like_k and like_pos to shape its empty views")
+        shape = list(like_k.shape)
+        shape[1] = 0
+        no_tokens = like_k.new_empty(shape)
+        return no_tokens, no_tokens, like_pos.new_empty((like_pos.shape[0], 0))
 
     def nbytes(self) -> int:
-        """Bytes of the cached tokens (the reserve excluded)."""
+        """Bytes of K and V that the cached tokens occupy (slots reserved past ``length`` are not counted)."""
         if self.k is None:
             return 0
-        per_token = (self.k[:, :, :1].numel() + self.v[:, :, :1].numel()) * self.k.element_size()
-        return per_token * self.length
+
+        def token_bytes(t: torch.Tensor) -> int:  # one token slot of a [B, H, capacity, D] buffer
+            return t.shape[0] * t.shape[1] * t.shape[3] * t.element_size()
+
+        return (token_bytes(self.k) + token_bytes(self.v)) * self.length
 
 
 class KVCache:
