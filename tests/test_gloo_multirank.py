@@ -44,7 +44,20 @@ def test_sequence_parallel_orchestration_matches_reference(golden_sp, ci):
         assert res["stats"]["sp.send"]["calls"] >= world - 1
 
 
-REFERENCE_ROOT = os.environ.get("COLLAB_INFER_REFERENCE", "/root/reference")
+def _reference_root() -> str:
+    """The unmodified reference: $COLLAB_INFER_REFERENCE, its offline install under baseline/_ref, or the source
+    tree BASELINE.json names, whichever holds collab_infer first ("" if none)."""
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    candidates = [os.environ.get("COLLAB_INFER_REFERENCE", ""), os.path.join(repo, "baseline", "_ref")]
+    try:
+        with open(os.path.join(repo, "BASELINE.json")) as f:
+            candidates.append(json.load(f).get("reference_path", ""))
+    except (OSError, ValueError):
+        pass
+    return next((c for c in candidates if c and os.path.isdir(os.path.join(c, "collab_infer"))), "")
+
+
+REFERENCE_ROOT = _reference_root()
 
 
 @pytest.mark.skipif(not os.path.isdir(os.path.join(REFERENCE_ROOT, "collab_infer")),
