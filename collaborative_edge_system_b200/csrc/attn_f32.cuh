@@ -1,17 +1,20 @@
 // fp32 attention with log-sum-exp for head dims 32 and 64 on the CUDA cores (collab_infer's config-1 precision: out
 // within 1e-4 and lse within 1e-5 of the reference's fp32 computation, parallel/attention.py:163-181).
 //
-// Register-tiled like a CUDA-core GEMM: a CTA (128 threads) owns 64-row blocks of one head's queries and walks
-// 64-key blocks staged in shared memory.  Under a causal mask the row blocks see very different key counts, so a
-// CTA takes two of them, the i-th from each end of the sequence, and every CTA has about the same work (the longest
-// CTA otherwise sets the launch's duration).  Thread (tr, tk) (tr = 0..15, tk = 0..7, the 8 tk of a tr in one warp) holds the scores
-// of rows tr + 16i (i = 0..3) against keys tk + 8j (j = 0..7) and the output of the same rows at columns
-// 4tk + 32c + e: each 16-byte shared-memory read then feeds 8 (scores) or 10.7 (output) FMAs on average instead of
-// 4, which is what bounds an untiled kernel (shared-memory wavefronts).  Per block: S = Q K^T into registers, the
-// position mask, the row max over the 8 threads of a row (shuffles), P = exp(S - m) into a transposed shared row
-// buffer (rows of a thread contiguous), O = O alpha + P V.  Each thread keeps a partial row sum; the 8 parts share
-// the row's max sequence and are added once at the end.  K/V blocks arrive by cp.async, two stages; only the
-// key blocks a CTA can see are loaded (a pre-pass over the key positions gives the first and last one).
+// Register-tiled like a CUDA-core GEMM: a CTA owns 64-row blocks of one head's queries and walks 64-key blocks
+// staged in shared memory with two groups of 4 warps, the even blocks in one and the odd ones in the other (each
+// group has its own K/V stages and its own online softmax; the two partial results of a row are merged exactly at
+// the end).  Under a causal mask the row blocks see very different key counts, so a CTA takes two of them, the
+// i-th from each end of the sequence, and every CTA has about the same work (the longest CTA otherwise sets the
+// launch's duration).  In a group, thread (tr, tk) (tr = 0..15, tk = 0..7, the 8 tk of a tr in one warp) holds
+// the scores of rows tr + 16i (i = 0..3) against keys tk + 8j (j = 0..7) and the output of the same rows at
+// columns 4tk + 32c + e: each 16-byte shared-memory read then feeds 8 (scores) or 10.7 (output) FMAs on average
+// instead of 4, which is what bounds an untiled kernel (shared-memory wavefronts).  Per block: S = Q K^T into
+// registers, the position mask, the row max over the 8 threads of a row (shuffles), P = exp(S - m) into a
+// transposed shared row buffer (rows of a thread contiguous), O = O alpha + P V.  Each thread keeps a partial row
+// sum; the 8 parts share the row's max sequence and are added once at the end.  K/V blocks arrive by cp.async,
+// two stages per group; only the key blocks a CTA can see are loaded (a pre-pass over the key positions gives the
+// first and last one).
 #pragma once
 
 #include "cea_common.cuh"
@@ -21,7 +24,8 @@ namespace cea {
 namespace f32k {
 
 constexpr int ROWS = 64;   // query rows per CTA
-constexpr int NT = 128;    // threads: 16 row groups x 8 key / column groups
+constexpr int GT = 128;    // threads of a key group: 16 row groups x 8 key / column groups
+constexpr int NT = 2 * GT; // two key groups: even and odd key blocks
 constexpr int BK = 64;     // keys per staged block
 constexpr int RI = 4;      // rows per thread (tr + 16 i)
 constexpr int KJ = 8;      // keys per thread per block (tk + 8 j)
@@ -39,7 +43,10 @@ struct Smem {
   static constexpr int Q = ROWS * STR;            // floats
   static constexpr int KV = STAGES * BK * STR;    // floats per tensor
   static constexpr int P = BK * PSTR;
-  static constexpr size_t BYTES = (Q + 2 * KV + P) * sizeof(float) + STAGES * BK * sizeof(long long);
+  static constexpr int GROUP = 2 * KV + P;       // floats of one key group: K and V stages, probability rows
+  static constexpr int X = RI * (D / 8) + 2 * RI;  // floats a thread hands over for the final merge
+  static constexpr size_t BYTES = (Q + 2 * GROUP) * sizeof(float) + 2 * STAGES * BK * sizeof(long long);
+  static_assert(GT * X <= KV, "the merge hand-over fits in a group's K stages");
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool in) {
@@ -53,24 +60,27 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // simt::Params carries the same operands (element strides); p.D == D
 template <int D>
-__global__ void __launch_bounds__(NT, 2) attn_f32_kernel(const simt::Params p) {
+__global__ void __launch_bounds__(NT, 1) attn_f32_kernel(const simt::Params p) {
   using S = Smem<D>;
   constexpr int STR = S::STR;
   constexpr int PSTR = S::PSTR;
   constexpr int DC = D / 32;  // 4-column groups per thread: columns 4 tk + 32 c + e
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int t = threadIdx.x;
+  const int g = t / GT;  // key group: blocks kb0 + g, kb0 + g + 2, ...
+  const int tg = t % GT;
   float* Qs = reinterpret_cast<float*>(smem_raw);  // [ROWS][STR], rows in query order
-  float* Ks = Qs + S::Q;
+  float* Ks = Qs + S::Q + g * S::GROUP;
   float* Vs = Ks + S::KV;
   float* Pt = Vs + S::KV;  // [BK][PSTR]: probability of key j for row tr + 16 i at j * PSTR + 4 tr + i
-  long long* kps = reinterpret_cast<long long*>(Pt + S::P);
+  long long* kps = reinterpret_cast<long long*>(Qs + S::Q + 2 * S::GROUP) + g * STAGES * BK;
+  float* handover = Qs + S::Q + S::GROUP;  // the odd group's K stages, once its loop is over
   __shared__ int s_range[2];
   __shared__ long long s_qmax;
 
-  const int t = threadIdx.x;
-  const int lane = t & 31;
+  const int lane = tg & 31;
   const int tk = lane & 7;
-  const int tr = (t >> 5) * 4 + (lane >> 3);
+  const int tr = (tg >> 5) * 4 + (lane >> 3);
   const int b = blockIdx.z;
   const int h = blockIdx.y;
   const int kvh = p.kv_map ? p.kv_map[h] : h / p.group;
@@ -159,8 +169,8 @@ __global__ void __launch_bounds__(NT, 2) attn_f32_kernel(const simt::Params p) {
   auto load_block = [&](int kb, int st) {
     const uint32_t ks = smem_u32(Ks + st * BK * STR), vs = smem_u32(Vs + st * BK * STR);
 #pragma unroll
-    for (int it = 0; it < (BK * D / 4) / NT; ++it) {
-      const int c = t + it * NT;  // chunk: key row c / (D/4), 4-float column group c % (D/4)
+    for (int it = 0; it < (BK * D / 4) / GT; ++it) {
+      const int c = tg + it * GT;  // chunk: key row c / (D/4), 4-float column group c % (D/4)
       const int row = c / (D / 4), col = (c % (D / 4)) * 4;
       const int kj = kb * BK + row;
       const bool in = kj < p.Sk;
@@ -169,23 +179,27 @@ __global__ void __launch_bounds__(NT, 2) attn_f32_kernel(const simt::Params p) {
       cp_async16(ks + so, kg + kjs * p.k_ss + col, in);
       cp_async16(vs + so, vg + kjs * p.v_ss + col, in);
     }
-    if (t < BK) {
-      const int kj = kb * BK + t;
-      kps[st * BK + t] = kj < p.Sk ? kpg[static_cast<int64_t>(kj) * p.kpos_ss] : -1ll;
+    if (tg < BK) {
+      const int kj = kb * BK + tg;
+      kps[st * BK + tg] = kj < p.Sk ? kpg[static_cast<int64_t>(kj) * p.kpos_ss] : -1ll;
     }
     cp_async_commit();
   };
 
-  if (kb0 <= kb1) load_block(kb0, 0);
-  for (int kb = kb0; kb <= kb1; ++kb) {
-    const int st = (kb - kb0) & 1;
-    if (kb < kb1) {
-      load_block(kb + 1, st ^ 1);
+  // this group's blocks: kb0 + g, kb0 + g + 2, ...; the group synchronises on its own named barrier
+  auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(GT) : "memory"); };
+  // (kb0 is INT_MAX when no block is visible: no arithmetic on it then)
+  const int kfirst = kb0 <= kb1 ? kb0 + g : 0, klast = kb0 <= kb1 ? kb1 : -1;
+  if (kfirst <= klast) load_block(kfirst, 0);
+  for (int kb = kfirst; kb <= klast; kb += 2) {
+    const int st = ((kb - kfirst) >> 1) & 1;
+    if (kb + 2 <= klast) {
+      load_block(kb + 2, st ^ 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();
+    group_sync();
     const float* Kb = Ks + st * BK * STR;
     const float* Vb = Vs + st * BK * STR;
     const long long* kpb = kps + st * BK;
@@ -263,14 +277,41 @@ __global__ void __launch_bounds__(NT, 2) attn_f32_kernel(const simt::Params p) {
         }
       }
     }
-    __syncthreads();  // the stage and the row buffer are rewritten in the next iteration
+    group_sync();  // the stage and the row buffer are rewritten in the next iteration
   }
 
-  // ---- epilogue: the row sums (8 parts, same max sequence), normalisation, the optional exact merge
+  // ---- the row sums (8 parts, same max sequence), then the odd group's rows merged into the even group's
 #pragma unroll
-  for (int i = 0; i < RI; ++i) {
+  for (int i = 0; i < RI; ++i)
 #pragma unroll
     for (int off = 1; off < 8; off <<= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], off);
+  float* x = handover + tg * S::X;
+  if (g == 1) {
+#pragma unroll
+    for (int i = 0; i < RI; ++i) {
+#pragma unroll
+      for (int d = 0; d < 4 * DC; ++d) x[i * 4 * DC + d] = o[i][d];
+      x[RI * 4 * DC + i] = m[i];
+      x[RI * 4 * DC + RI + i] = l[i];
+    }
+  }
+  __syncthreads();
+  if (g == 1) continue;  // the even group writes the rows
+#pragma unroll
+  for (int i = 0; i < RI; ++i) {
+    const float m1 = x[RI * 4 * DC + i], l1 = x[RI * 4 * DC + RI + i];
+    const float mm = fmaxf(m[i], m1);
+    const float w0 = m[i] == -INFINITY ? 0.f : expf(m[i] - mm);
+    const float w1 = m1 == -INFINITY ? 0.f : expf(m1 - mm);
+    l[i] = l[i] * w0 + l1 * w1;
+    m[i] = mm;
+#pragma unroll
+    for (int d = 0; d < 4 * DC; ++d) o[i][d] = o[i][d] * w0 + x[i * 4 * DC + d] * w1;
+  }
+
+  // ---- epilogue: normalisation, the optional exact merge into the stored result
+#pragma unroll
+  for (int i = 0; i < RI; ++i) {
     const int qi = q0 + tr + 16 * i;
     if (qi >= p.Sq) continue;
     const float lse_row = l[i] > 0.f ? m[i] + logf(l[i]) : -INFINITY;
