@@ -90,259 +90,260 @@ __global__ void __launch_bounds__(NT, 1) attn_f32_kernel(const simt::Params p) {
   const int far = causal ? nblk - 1 - near : near;
 
   for (int pass = 0; pass < 2; ++pass) {
-  if (pass == 1 && near == far) break;
-  const int q0 = (pass == 0 ? far : near) * ROWS;
+    if (pass == 1 && near == far) break;
+    const int q0 = (pass == 0 ? far : near) * ROWS;
 
-  // ---- this thread's rows and their positions
-  long long qpos[RI];
+    // ---- this thread's rows and their positions
+    long long qpos[RI];
 #pragma unroll
-  for (int i = 0; i < RI; ++i) {
-    const int qi = q0 + tr + 16 * i;
-    qpos[i] = qi < p.Sq ? p.q_pos[b * p.qpos_sb + static_cast<int64_t>(qi) * p.qpos_ss] : -1ll;
-  }
+    for (int i = 0; i < RI; ++i) {
+      const int qi = q0 + tr + 16 * i;
+      qpos[i] = qi < p.Sq ? p.q_pos[b * p.qpos_sb + static_cast<int64_t>(qi) * p.qpos_ss] : -1ll;
+    }
 
-  // ---- the CTA's visible key blocks: [first, last] over keys with 0 <= kpos (<= max q position when causal)
-  __syncthreads();  // the previous row block's readers of the shared state are done
-  if (t == 0) {
-    s_range[0] = INT_MAX;
-    s_range[1] = -1;
-    s_qmax = -1;
-  }
-  __syncthreads();
-  if (tk == 0) {
-    long long mx = -1;
+    // ---- the CTA's visible key blocks: [first, last] over keys with 0 <= kpos (<= max q position when causal)
+    __syncthreads();  // the previous row block's readers of the shared state are done
+    if (t == 0) {
+      s_range[0] = INT_MAX;
+      s_range[1] = -1;
+      s_qmax = -1;
+    }
+    __syncthreads();
+    if (tk == 0) {
+      long long mx = -1;
 #pragma unroll
-    for (int i = 0; i < RI; ++i)
-      if (q0 + tr + 16 * i < p.Sq) mx = max(mx, qpos[i]);
-    atomicMax(&s_qmax, mx);
-  }
-  __syncthreads();
-  const long long qmax = s_qmax;
-  {
-    int first = INT_MAX, last = -1;
-    const int64_t* kp = p.k_pos + b * p.kpos_sb;
-    for (int j = t; j < p.Sk; j += NT) {
-      const long long v = kp[static_cast<int64_t>(j) * p.kpos_ss];
-      if (v >= 0 && (!causal || v <= qmax)) {
-        first = min(first, j / BK);
-        last = max(last, j / BK);
+      for (int i = 0; i < RI; ++i)
+        if (q0 + tr + 16 * i < p.Sq) mx = max(mx, qpos[i]);
+      atomicMax(&s_qmax, mx);
+    }
+    __syncthreads();
+    const long long qmax = s_qmax;
+    {
+      int first = INT_MAX, last = -1;
+      const int64_t* kp = p.k_pos + b * p.kpos_sb;
+      for (int j = t; j < p.Sk; j += NT) {
+        const long long v = kp[static_cast<int64_t>(j) * p.kpos_ss];
+        if (v >= 0 && (!causal || v <= qmax)) {
+          first = min(first, j / BK);
+          last = max(last, j / BK);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        first = min(first, __shfl_xor_sync(0xffffffffu, first, off));
+        last = max(last, __shfl_xor_sync(0xffffffffu, last, off));
+      }
+      if (lane == 0) {
+        atomicMin(&s_range[0], first);
+        atomicMax(&s_range[1], last);
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      first = min(first, __shfl_xor_sync(0xffffffffu, first, off));
-      last = max(last, __shfl_xor_sync(0xffffffffu, last, off));
-    }
-    if (lane == 0) {
-      atomicMin(&s_range[0], first);
-      atomicMax(&s_range[1], last);
-    }
-  }
 
-  // ---- the CTA's query rows into shared memory (zero past Sq)
-  {
-    const float* qg = reinterpret_cast<const float*>(p.q) + b * p.q_sb + h * p.q_sh;
-    for (int e = t; e < ROWS * D; e += NT) {
-      const int row = e / D, d = e % D;
-      const int qi = q0 + row;
-      Qs[row * STR + d] = qi < p.Sq ? qg[static_cast<int64_t>(qi) * p.q_ss + d] : 0.f;
+    // ---- the CTA's query rows into shared memory (zero past Sq)
+    {
+      const float* qg = reinterpret_cast<const float*>(p.q) + b * p.q_sb + h * p.q_sh;
+      for (int e = t; e < ROWS * D; e += NT) {
+        const int row = e / D, d = e % D;
+        const int qi = q0 + row;
+        Qs[row * STR + d] = qi < p.Sq ? qg[static_cast<int64_t>(qi) * p.q_ss + d] : 0.f;
+      }
     }
-  }
-  __syncthreads();
-  const int kb0 = s_range[0], kb1 = s_range[1];
+    __syncthreads();
+    const int kb0 = s_range[0], kb1 = s_range[1];
 
-  float o[RI][4 * DC];  // o[i][4c + e]: row tr + 16 i, column 4 tk + 32 c + e
-  float m[RI], l[RI];
+    float o[RI][4 * DC];  // o[i][4c + e]: row tr + 16 i, column 4 tk + 32 c + e
+    float m[RI], l[RI];
 #pragma unroll
-  for (int i = 0; i < RI; ++i) {
-    m[i] = -INFINITY;
-    l[i] = 0.f;
+    for (int i = 0; i < RI; ++i) {
+      m[i] = -INFINITY;
+      l[i] = 0.f;
 #pragma unroll
-    for (int d = 0; d < 4 * DC; ++d) o[i][d] = 0.f;
-  }
-  const float scale = static_cast<float>(p.scale);
-
-  const float* kg = reinterpret_cast<const float*>(p.k) + b * p.k_sb + kvh * p.k_sh;
-  const float* vg = reinterpret_cast<const float*>(p.v) + b * p.v_sb + kvh * p.v_sh;
-  const int64_t* kpg = p.k_pos + b * p.kpos_sb;
-  // block kb into stage st: BK rows x D/4 chunks of 16 bytes for K and for V; positions by BK threads
-  auto load_block = [&](int kb, int st) {
-    const uint32_t ks = smem_u32(Ks + st * BK * STR), vs = smem_u32(Vs + st * BK * STR);
-#pragma unroll
-    for (int it = 0; it < (BK * D / 4) / GT; ++it) {
-      const int c = tg + it * GT;  // chunk: key row c / (D/4), 4-float column group c % (D/4)
-      const int row = c / (D / 4), col = (c % (D / 4)) * 4;
-      const int kj = kb * BK + row;
-      const bool in = kj < p.Sk;
-      const int64_t kjs = in ? kj : 0;
-      const uint32_t so = static_cast<uint32_t>((row * STR + col) * sizeof(float));
-      cp_async16(ks + so, kg + kjs * p.k_ss + col, in);
-      cp_async16(vs + so, vg + kjs * p.v_ss + col, in);
+      for (int d = 0; d < 4 * DC; ++d) o[i][d] = 0.f;
     }
-    if (tg < BK) {
-      const int kj = kb * BK + tg;
-      kps[st * BK + tg] = kj < p.Sk ? kpg[static_cast<int64_t>(kj) * p.kpos_ss] : -1ll;
-    }
-    cp_async_commit();
-  };
+    const float scale = static_cast<float>(p.scale);
 
-  // this group's blocks: kb0 + g, kb0 + g + 2, ...; the group synchronises on its own named barrier
-  auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(GT) : "memory"); };
-  // (kb0 is INT_MAX when no block is visible: no arithmetic on it then)
-  const int kfirst = kb0 <= kb1 ? kb0 + g : 0, klast = kb0 <= kb1 ? kb1 : -1;
-  if (kfirst <= klast) load_block(kfirst, 0);
-  for (int kb = kfirst; kb <= klast; kb += 2) {
-    const int st = ((kb - kfirst) >> 1) & 1;
-    if (kb + 2 <= klast) {
-      load_block(kb + 2, st ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    group_sync();
-    const float* Kb = Ks + st * BK * STR;
-    const float* Vb = Vs + st * BK * STR;
-    const long long* kpb = kps + st * BK;
+    const float* kg = reinterpret_cast<const float*>(p.k) + b * p.k_sb + kvh * p.k_sh;
+    const float* vg = reinterpret_cast<const float*>(p.v) + b * p.v_sb + kvh * p.v_sh;
+    const int64_t* kpg = p.k_pos + b * p.kpos_sb;
+    // block kb into stage st: BK rows x D/4 chunks of 16 bytes for K and for V; positions by BK threads
+    auto load_block = [&](int kb, int st) {
+      const uint32_t ks = smem_u32(Ks + st * BK * STR), vs = smem_u32(Vs + st * BK * STR);
+#pragma unroll
+      for (int it = 0; it < (BK * D / 4) / GT; ++it) {
+        const int c = tg + it * GT;  // chunk: key row c / (D/4), 4-float column group c % (D/4)
+        const int row = c / (D / 4), col = (c % (D / 4)) * 4;
+        const int kj = kb * BK + row;
+        const bool in = kj < p.Sk;
+        const int64_t kjs = in ? kj : 0;
+        const uint32_t so = static_cast<uint32_t>((row * STR + col) * sizeof(float));
+        cp_async16(ks + so, kg + kjs * p.k_ss + col, in);
+        cp_async16(vs + so, vg + kjs * p.v_ss + col, in);
+      }
+      if (tg < BK) {
+        const int kj = kb * BK + tg;
+        kps[st * BK + tg] = kj < p.Sk ? kpg[static_cast<int64_t>(kj) * p.kpos_ss] : -1ll;
+      }
+      cp_async_commit();
+    };
 
-    // S tile: rows tr + 16 i, keys tk + 8 j
-    float s[RI][KJ];
-#pragma unroll
-    for (int i = 0; i < RI; ++i)
-#pragma unroll
-      for (int j = 0; j < KJ; ++j) s[i][j] = 0.f;
-#pragma unroll 4
-    for (int d4 = 0; d4 < D / 4; ++d4) {
-      float4 qv[RI], kv[KJ];
-#pragma unroll
-      for (int i = 0; i < RI; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (tr + 16 * i) * STR + 4 * d4);
-#pragma unroll
-      for (int j = 0; j < KJ; ++j) kv[j] = *reinterpret_cast<const float4*>(Kb + (tk + 8 * j) * STR + 4 * d4);
+    // this group's blocks: kb0 + g, kb0 + g + 2, ...; the group synchronises on its own named barrier
+    auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(GT) : "memory"); };
+    // (kb0 is INT_MAX when no block is visible: no arithmetic on it then)
+    const int kfirst = kb0 <= kb1 ? kb0 + g : 0, klast = kb0 <= kb1 ? kb1 : -1;
+    if (kfirst <= klast) load_block(kfirst, 0);
+    for (int kb = kfirst; kb <= klast; kb += 2) {
+      const int st = ((kb - kfirst) >> 1) & 1;
+      if (kb + 2 <= klast) {
+        load_block(kb + 2, st ^ 1);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      group_sync();
+      const float* Kb = Ks + st * BK * STR;
+      const float* Vb = Vs + st * BK * STR;
+      const long long* kpb = kps + st * BK;
+
+      // S tile: rows tr + 16 i, keys tk + 8 j
+      float s[RI][KJ];
 #pragma unroll
       for (int i = 0; i < RI; ++i)
 #pragma unroll
-        for (int j = 0; j < KJ; ++j) {
-          s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
-          s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
-          s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
-          s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
-        }
-    }
-
-    // mask, the row max over the row's 8 threads, probabilities into the transposed row buffer
-    long long kp[KJ];
-#pragma unroll
-    for (int j = 0; j < KJ; ++j) kp[j] = kpb[tk + 8 * j];
-#pragma unroll
-    for (int i = 0; i < RI; ++i) {
-      float mb = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < KJ; ++j) {
-        const bool vis = kp[j] >= 0 && (!causal || kp[j] <= qpos[i]);
-        s[i][j] = vis ? s[i][j] * scale : -INFINITY;
-        mb = fmaxf(mb, s[i][j]);
-      }
-#pragma unroll
-      for (int off = 1; off < 8; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-      const float m_new = fmaxf(m[i], mb);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row that has seen nothing keeps p = 0
-      const float alpha = expf(m[i] - m_use);                 // 0 while the row has seen nothing
-      m[i] = m_new;
-      float rs = 0.f;
-#pragma unroll
-      for (int j = 0; j < KJ; ++j) {
-        const float pj = expf(s[i][j] - m_use);
-        rs += pj;
-        Pt[(tk + 8 * j) * PSTR + 4 * tr + i] = pj;
-      }
-      l[i] = l[i] * alpha + rs;  // this thread's part of the row sum
-#pragma unroll
-      for (int d = 0; d < 4 * DC; ++d) o[i][d] *= alpha;
-    }
-    __syncwarp();  // a row's probabilities come from the 8 threads of its row group, all in this warp
-
-    // O += P V over the block's keys: 4 probabilities (one 16-byte read) x 4 DC columns per key
+        for (int j = 0; j < KJ; ++j) s[i][j] = 0.f;
 #pragma unroll 4
-    for (int j = 0; j < BK; ++j) {
-      const float4 pv = *reinterpret_cast<const float4*>(Pt + j * PSTR + 4 * tr);
-      const float pr[RI] = {pv.x, pv.y, pv.z, pv.w};
+      for (int d4 = 0; d4 < D / 4; ++d4) {
+        float4 qv[RI], kv[KJ];
 #pragma unroll
-      for (int c = 0; c < DC; ++c) {
-        const float4 vv = *reinterpret_cast<const float4*>(Vb + j * STR + 4 * tk + 32 * c);
+        for (int i = 0; i < RI; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (tr + 16 * i) * STR + 4 * d4);
 #pragma unroll
-        for (int i = 0; i < RI; ++i) {
-          o[i][4 * c + 0] = fmaf(pr[i], vv.x, o[i][4 * c + 0]);
-          o[i][4 * c + 1] = fmaf(pr[i], vv.y, o[i][4 * c + 1]);
-          o[i][4 * c + 2] = fmaf(pr[i], vv.z, o[i][4 * c + 2]);
-          o[i][4 * c + 3] = fmaf(pr[i], vv.w, o[i][4 * c + 3]);
+        for (int j = 0; j < KJ; ++j) kv[j] = *reinterpret_cast<const float4*>(Kb + (tk + 8 * j) * STR + 4 * d4);
+#pragma unroll
+        for (int i = 0; i < RI; ++i)
+#pragma unroll
+          for (int j = 0; j < KJ; ++j) {
+            s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+            s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+            s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+            s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+          }
+      }
+
+      // mask, the row max over the row's 8 threads, probabilities into the transposed row buffer
+      long long kp[KJ];
+#pragma unroll
+      for (int j = 0; j < KJ; ++j) kp[j] = kpb[tk + 8 * j];
+#pragma unroll
+      for (int i = 0; i < RI; ++i) {
+        float mb = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < KJ; ++j) {
+          const bool vis = kp[j] >= 0 && (!causal || kp[j] <= qpos[i]);
+          s[i][j] = vis ? s[i][j] * scale : -INFINITY;
+          mb = fmaxf(mb, s[i][j]);
+        }
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        const float m_new = fmaxf(m[i], mb);
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row that has seen nothing keeps p = 0
+        const float alpha = expf(m[i] - m_use);                 // 0 while the row has seen nothing
+        m[i] = m_new;
+        float rs = 0.f;
+#pragma unroll
+        for (int j = 0; j < KJ; ++j) {
+          const float pj = expf(s[i][j] - m_use);
+          rs += pj;
+          Pt[(tk + 8 * j) * PSTR + 4 * tr + i] = pj;
+        }
+        l[i] = l[i] * alpha + rs;  // this thread's part of the row sum
+#pragma unroll
+        for (int d = 0; d < 4 * DC; ++d) o[i][d] *= alpha;
+      }
+      __syncwarp();  // a row's probabilities come from the 8 threads of its row group, all in this warp
+
+      // O += P V over the block's keys: 4 probabilities (one 16-byte read) x 4 DC columns per key
+#pragma unroll 4
+      for (int j = 0; j < BK; ++j) {
+        const float4 pv = *reinterpret_cast<const float4*>(Pt + j * PSTR + 4 * tr);
+        const float pr[RI] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+        for (int c = 0; c < DC; ++c) {
+          const float4 vv = *reinterpret_cast<const float4*>(Vb + j * STR + 4 * tk + 32 * c);
+#pragma unroll
+          for (int i = 0; i < RI; ++i) {
+            o[i][4 * c + 0] = fmaf(pr[i], vv.x, o[i][4 * c + 0]);
+            o[i][4 * c + 1] = fmaf(pr[i], vv.y, o[i][4 * c + 1]);
+            o[i][4 * c + 2] = fmaf(pr[i], vv.z, o[i][4 * c + 2]);
+            o[i][4 * c + 3] = fmaf(pr[i], vv.w, o[i][4 * c + 3]);
+          }
         }
       }
+      group_sync();  // the stage and the row buffer are rewritten in the next iteration
     }
-    group_sync();  // the stage and the row buffer are rewritten in the next iteration
-  }
 
-  // ---- the row sums (8 parts, same max sequence), then the odd group's rows merged into the even group's
+    // ---- the row sums (8 parts, same max sequence), then the odd group's rows merged into the even group's
 #pragma unroll
-  for (int i = 0; i < RI; ++i)
+    for (int i = 0; i < RI; ++i)
 #pragma unroll
-    for (int off = 1; off < 8; off <<= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], off);
-  float* x = handover + tg * S::X;
-  if (g == 1) {
+      for (int off = 1; off < 8; off <<= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], off);
+    float* x = handover + tg * S::X;
+    if (g == 1) {
+#pragma unroll
+      for (int i = 0; i < RI; ++i) {
+#pragma unroll
+        for (int d = 0; d < 4 * DC; ++d) x[i * 4 * DC + d] = o[i][d];
+        x[RI * 4 * DC + i] = m[i];
+        x[RI * 4 * DC + RI + i] = l[i];
+      }
+    }
+    __syncthreads();
+    if (g == 1) continue;  // the even group writes the rows
 #pragma unroll
     for (int i = 0; i < RI; ++i) {
+      const float m1 = x[RI * 4 * DC + i], l1 = x[RI * 4 * DC + RI + i];
+      const float mm = fmaxf(m[i], m1);
+      const float w0 = m[i] == -INFINITY ? 0.f : expf(m[i] - mm);
+      const float w1 = m1 == -INFINITY ? 0.f : expf(m1 - mm);
+      l[i] = l[i] * w0 + l1 * w1;
+      m[i] = mm;
 #pragma unroll
-      for (int d = 0; d < 4 * DC; ++d) x[i * 4 * DC + d] = o[i][d];
-      x[RI * 4 * DC + i] = m[i];
-      x[RI * 4 * DC + RI + i] = l[i];
+      for (int d = 0; d < 4 * DC; ++d) o[i][d] = o[i][d] * w0 + x[i * 4 * DC + d] * w1;
     }
-  }
-  __syncthreads();
-  if (g == 1) continue;  // the even group writes the rows
-#pragma unroll
-  for (int i = 0; i < RI; ++i) {
-    const float m1 = x[RI * 4 * DC + i], l1 = x[RI * 4 * DC + RI + i];
-    const float mm = fmaxf(m[i], m1);
-    const float w0 = m[i] == -INFINITY ? 0.f : expf(m[i] - mm);
-    const float w1 = m1 == -INFINITY ? 0.f : expf(m1 - mm);
-    l[i] = l[i] * w0 + l1 * w1;
-    m[i] = mm;
-#pragma unroll
-    for (int d = 0; d < 4 * DC; ++d) o[i][d] = o[i][d] * w0 + x[i * 4 * DC + d] * w1;
-  }
 
-  // ---- epilogue: normalisation, the optional exact merge into the stored result
+    // ---- epilogue: normalisation, the optional exact merge into the stored result
 #pragma unroll
-  for (int i = 0; i < RI; ++i) {
-    const int qi = q0 + tr + 16 * i;
-    if (qi >= p.Sq) continue;
-    const float lse_row = l[i] > 0.f ? m[i] + logf(l[i]) : -INFINITY;
-    const float inv_l = l[i] > 0.f ? 1.f / l[i] : 0.f;
-    float w_old = 0.f, w_new = 1.f, lse_out = lse_row;
-    float* lse_ptr = p.lse ? reinterpret_cast<float*>(p.lse) + b * p.l_sb + h * p.l_sh + static_cast<int64_t>(qi) * p.l_ss
-                           : nullptr;
-    if (p.accumulate) {
-      const float lse_old = *lse_ptr;
-      const float mx = fmaxf(lse_old, lse_row);
-      if (mx == -INFINITY) {
-        lse_out = -INFINITY;
-        w_new = 0.f;
-      } else {
-        lse_out = mx + log1pf(expf(-fabsf(lse_old - lse_row)));
-        w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - lse_out);
-        w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - lse_out);
+    for (int i = 0; i < RI; ++i) {
+      const int qi = q0 + tr + 16 * i;
+      if (qi >= p.Sq) continue;
+      const float lse_row = l[i] > 0.f ? m[i] + logf(l[i]) : -INFINITY;
+      const float inv_l = l[i] > 0.f ? 1.f / l[i] : 0.f;
+      float w_old = 0.f, w_new = 1.f, lse_out = lse_row;
+      float* lse_ptr = p.lse ? reinterpret_cast<float*>(p.lse) + b * p.l_sb + h * p.l_sh +
+                                   static_cast<int64_t>(qi) * p.l_ss
+                             : nullptr;
+      if (p.accumulate) {
+        const float lse_old = *lse_ptr;
+        const float mx = fmaxf(lse_old, lse_row);
+        if (mx == -INFINITY) {
+          lse_out = -INFINITY;
+          w_new = 0.f;
+        } else {
+          lse_out = mx + log1pf(expf(-fabsf(lse_old - lse_row)));
+          w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - lse_out);
+          w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - lse_out);
+        }
       }
+      float* og = reinterpret_cast<float*>(p.out) + b * p.o_sb + static_cast<int64_t>(qi) * p.o_ss + h * p.o_sh;
+#pragma unroll
+      for (int c = 0; c < DC; ++c)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = 4 * tk + 32 * c + e;
+          float val = o[i][4 * c + e] * inv_l * w_new;
+          if (p.accumulate) val += og[d] * w_old;
+          og[d] = val;
+        }
+      if (tk == 0 && lse_ptr) *lse_ptr = lse_out;
     }
-    float* og = reinterpret_cast<float*>(p.out) + b * p.o_sb + static_cast<int64_t>(qi) * p.o_ss + h * p.o_sh;
-#pragma unroll
-    for (int c = 0; c < DC; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = 4 * tk + 32 * c + e;
-        float val = o[i][4 * c + e] * inv_l * w_new;
-        if (p.accumulate) val += og[d] * w_old;
-        og[d] = val;
-      }
-    if (tk == 0 && lse_ptr) *lse_ptr = lse_out;
-  }
   }  // row blocks
 }
 
